@@ -1,0 +1,134 @@
+"""ctypes binding of the C ABI in ``include/b200_gemm.h`` (libb200gemm.so).
+
+This is the boundary the parity tests and the end-to-end bench call: plain
+pointers, sizes and a stream handle, a status code back.  Loading fails
+loudly when the library has not been built -- there is no fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libb200gemm.so"
+
+# Status codes (include/b200_gemm.h).
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_ALIGNMENT = 2
+ERR_UNSUPPORTED_DEVICE = 3
+ERR_TENSOR_MAP = 4
+ERR_LAUNCH = 5
+ERR_DEVICE_TIMEOUT = 6
+ERR_TOO_LARGE = 7
+
+# Device error-word values written by a pipeline wait that ran out.
+DEVICE_WAIT_CODES = {
+    0x1001: "producer wait on a ring slot",
+    0x1002: "MMA wait on TMA data",
+    0x1003: "MMA wait on the epilogue",
+    0x1004: "epilogue wait on the MMA",
+    0x1005: "final MMA drain",
+    0x1006: "wait probe",
+}
+
+# Every symbol the header declares, with (restype, argtypes).
+_vp, _i, _u32, _u64, _ull = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, \
+    ctypes.c_ulonglong
+_ip = ctypes.POINTER(ctypes.c_int)
+SIGNATURES = {
+    "b200_gemm_bf16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "b200_gemm_bf16_profile": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp]),
+    "b200_gemm_profile_rows": (_i, [_i, _i, _i, _ip]),
+    "b200_gemm_device_status": (_i, [_i, _ip]),
+    "b200_gemm_set_wait_timeout_ns": (_i, [_ull]),
+    "b200_gemm_wait_probe": (_i, [_ull, _vp]),
+    "b200_gemm_status_string": (ctypes.c_char_p, [_i]),
+    "b200_gemm_tile_coord": (None, [_i, _i, _i, _i, _ip, _ip]),
+    "b200_gemm_idesc": (_u32, [_i, _i]),
+    "b200_gemm_smem_desc": (_u64, [_u32]),
+    "b200_gemm_launch_shape": (_i, [_i, _i, _i, _ip, _ip, _ip, _ip]),
+}
+
+_lib = None
+
+
+class GemmError(RuntimeError):
+    def __init__(self, status: int, what: str = "b200_gemm"):
+        self.status = status
+        super().__init__(f"{what}: {status_string(status)} (status {status})")
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH.name} is not built; run `python -m blackwell_gemm_b200.build`")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return lib().b200_gemm_status_string(int(status)).decode()
+
+
+def check(status: int, what: str = "b200_gemm") -> None:
+    if status != OK:
+        raise GemmError(status, what)
+
+
+def gemm_bf16(a_ptr: int, b_ptr: int, c_ptr: int, M: int, N: int, K: int, lda: int, ldb: int,
+              ldc: int, stream: int = 0) -> int:
+    """Raw C-ABI call: returns the status code (does not raise)."""
+    return lib().b200_gemm_bf16(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, stream)
+
+
+def gemm_bf16_profile(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, prof_ptr, entries,
+                      stream=0) -> int:
+    return lib().b200_gemm_bf16_profile(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, prof_ptr,
+                                        entries, stream)
+
+
+def profile_rows(M: int, N: int, K: int) -> int:
+    rows = ctypes.c_int(0)
+    check(lib().b200_gemm_profile_rows(M, N, K, ctypes.byref(rows)), "profile_rows")
+    return rows.value
+
+
+def device_status(clear: bool = True) -> int:
+    v = ctypes.c_int(0)
+    check(lib().b200_gemm_device_status(1 if clear else 0, ctypes.byref(v)), "device_status")
+    return v.value
+
+
+def set_wait_timeout_ns(ns: int) -> None:
+    check(lib().b200_gemm_set_wait_timeout_ns(int(ns)), "set_wait_timeout_ns")
+
+
+def wait_probe(timeout_ns: int, stream: int = 0) -> int:
+    return lib().b200_gemm_wait_probe(int(timeout_ns), stream)
+
+
+def tile_coord(t: int, tiles_m: int, tiles_n: int, group: int):
+    tm, tn = ctypes.c_int(0), ctypes.c_int(0)
+    lib().b200_gemm_tile_coord(t, tiles_m, tiles_n, group, ctypes.byref(tm), ctypes.byref(tn))
+    return tm.value, tn.value
+
+
+def idesc(mma_m: int, mma_n: int) -> int:
+    return lib().b200_gemm_idesc(mma_m, mma_n)
+
+
+def smem_desc(addr: int) -> int:
+    return lib().b200_gemm_smem_desc(addr)
+
+
+def launch_shape(M: int, N: int, K: int) -> dict:
+    t, g, s, th = (ctypes.c_int(0) for _ in range(4))
+    check(lib().b200_gemm_launch_shape(M, N, K, ctypes.byref(t), ctypes.byref(g), ctypes.byref(s),
+                                       ctypes.byref(th)), "launch_shape")
+    return {"tiles": t.value, "grid": g.value, "smem_bytes": s.value, "threads": th.value}

@@ -1,0 +1,405 @@
+// Persistent, warp-specialised BF16 GEMM for sm_100a:  C = A * B^T
+//   A  M x K bf16, row stride lda (K-major)
+//   B  N x K bf16, row stride ldb (K-major; the reference's "(K,N) view of an
+//      N x K buffer", matmul.cpp:25-39)
+//   C  M x N bf16, row stride ldc, fp32 accumulation, round-to-nearest-even
+//
+// One 2-CTA cluster ("pair") owns a 256x256 tile of C at a time.  Warp roles
+// per CTA (192 threads):
+//   warp 0     TMA producer: fills a 6-stage ring of {A 128x64, B 128x64}
+//   warp 1     TMEM owner; in the pair leader also the MMA issuer
+//              (tcgen05.mma.cta_group::2, 4 x K16 per stage)
+//   warps 2-5  epilogue: tcgen05.ld -> bf16 -> swizzled smem -> TMA store,
+//              one warp per TMEM lane quarter, each with its own two
+//              4 KiB staging buffers so no epilogue warp waits for another
+// Pipelines:
+//   full[s]/empty[s]        ring stage s (full lives in the leader: both
+//                           producers arrive on it; empty lives in each CTA)
+//   acc_full[b]/acc_empty[b] TMEM accumulator buffer b (2 buffers), so the
+//                           epilogue of tile i overlaps the MMAs of tile i+1
+// Reference behaviour followed: kernel_v8.cu:360-773 (same math, same tile,
+// same TMA/UMMA/epilogue data path); the scheduling here is a static
+// persistent walk over a grouped raster (gemm_layout.h) instead of cluster
+// launch control, and every wait is bounded (a stuck pipeline records an
+// error code in `status` and the kernel returns instead of spinning).
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "gemm_layout.h"
+#include "sm100_ptx.cuh"
+
+namespace b200 {
+
+struct GemmArgs {
+  int M, N, K;
+  int tiles_m, tiles_n, k_blocks, group;
+  int* status;                    // device error word (0 = ok)
+  unsigned long long timeout_ns;  // bound on any single pipeline wait
+  long long* prof;                // intra-kernel profiler rows (nullptr: off)
+  int prof_entries;
+};
+
+// Error codes written to GemmArgs::status by a wait that ran out.
+enum : int {
+  kErrWaitEmpty = 0x1001,     // producer waited on a ring slot
+  kErrWaitFull = 0x1002,      // MMA waited on TMA data
+  kErrWaitAccEmpty = 0x1003,  // MMA waited on the epilogue to free TMEM
+  kErrWaitAccFull = 0x1004,   // epilogue waited on the MMA
+  kErrWaitDrain = 0x1005,     // final wait for outstanding MMAs
+  kErrWaitProbe = 0x1006,     // self-test kernel (wait that nothing releases)
+};
+
+// Intra-kernel profiler tags; numbering and row format follow the
+// reference's profiler.h:4-13,22-50 (row = [count, (smid, tag, start_ns,
+// duration_ns) x entries]).  Recording stops when a row is full.
+enum ProfTag : int {
+  kTagSetup = 0, kTagIssueTMA, kTagIssueMMA, kTagWaitTMA, kTagWaitMMA,
+  kTagWaitMainloop, kTagWaitEpilogue, kTagEpilogue,
+};
+
+template <bool kOn>
+struct Prof {
+  long long* row = nullptr;
+  int cap = 0, cnt = 0, sm = 0;
+  long long t0 = 0;
+  int tag = 0;
+  __device__ __forceinline__ void init(long long* base, int entries, int row_idx) {
+    if constexpr (kOn) {
+      row = base + (long long)row_idx * (1 + 4 * entries);
+      cap = entries;
+      sm = (int)smid();
+    }
+  }
+  __device__ __forceinline__ void start(int t) {
+    if constexpr (kOn) { tag = t; t0 = (long long)globaltimer_ns(); }
+  }
+  __device__ __forceinline__ void stop() {
+    if constexpr (kOn) {
+      if (cnt < cap) {
+        long long* e = row + 1 + 4 * cnt;
+        e[0] = sm; e[1] = tag; e[2] = t0; e[3] = (long long)globaltimer_ns() - t0;
+        ++cnt;
+      }
+    }
+  }
+  __device__ __forceinline__ void flush() {
+    if constexpr (kOn) row[0] = cnt;
+  }
+};
+
+struct WaitCtx {
+  int* status;
+  unsigned long long timeout_ns;
+  uint32_t abort_local;  // shared::cta address of this CTA's abort word
+  uint32_t abort_peer;   // shared::cluster address of the peer's abort word
+};
+
+__device__ __forceinline__ uint32_t ld_volatile_shared(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Wait for `parity` on a local mbarrier.  Gives up when the abort word is set
+// (another warp of the pair already gave up) or after timeout_ns; in the
+// latter case it records `code`, raises both CTAs' abort words and returns
+// false so the caller can leave its loop and reach the teardown.
+__device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, const WaitCtx& w, int code,
+                                       bool honour_abort) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spin & 15u) == 0) {
+      if (honour_abort && ld_volatile_shared(w.abort_local) != 0) return false;
+      if (globaltimer_ns() - t0 > w.timeout_ns) {
+        atomicCAS(w.status, 0, code);
+        asm volatile("st.volatile.shared.u32 [%0], %1;" :: "r"(w.abort_local), "r"(1u) : "memory");
+        st_cluster_u32(w.abort_peer, 1u);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, const WaitCtx& w,
+                                             int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return wait_slow(bar, parity, w, code, true);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(lo), __uint_as_float(hi));
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <bool kProfile>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                      const __grid_constant__ CUtensorMap tmap_b,
+                      const __grid_constant__ CUtensorMap tmap_c,
+                      const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ alignas(8) uint64_t bar_full[kStages];
+  __shared__ alignas(8) uint64_t bar_empty[kStages];
+  __shared__ alignas(8) uint64_t bar_acc_full[kAccBufs];
+  __shared__ alignas(8) uint64_t bar_acc_empty[kAccBufs];
+  __shared__ alignas(8) uint64_t bar_drain;
+  __shared__ uint32_t tmem_slot;
+  __shared__ uint32_t abort_word;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int tiles = args.tiles_m * args.tiles_n;
+
+  // 1 KiB aligned start: the 128 B swizzle atoms (8 rows x 128 B) must be.
+  const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t store_base = smem_base + kStages * kStageBytes;
+
+  Prof<kProfile> prof;
+  if constexpr (kProfile) {
+    if (lane == 0) {
+      prof.init(args.prof, args.prof_entries, blockIdx.x * kWarps + warp);
+      prof.start(kTagSetup);
+    }
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&bar_full[s]), 2);   // one expect_tx arrive per CTA
+      mbar_init(smem_u32(&bar_empty[s]), 1);  // one tcgen05.commit
+    }
+    for (int b = 0; b < kAccBufs; ++b) {
+      mbar_init(smem_u32(&bar_acc_full[b]), 1);
+      mbar_init(smem_u32(&bar_acc_empty[b]), 2 * kEpiWarps);  // every epilogue warp of the pair
+    }
+    mbar_init(smem_u32(&bar_drain), 1);
+    abort_word = 0;
+    fence_mbar_init_cluster();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_c);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(&tmem_slot), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before_sync();
+  cluster_sync_all();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = tmem_slot;
+
+  WaitCtx wctx;
+  wctx.status = args.status;
+  wctx.timeout_ns = args.timeout_ns;
+  wctx.abort_local = smem_u32(&abort_word);
+  wctx.abort_peer = cluster_map(smem_u32(&abort_word), rank ^ 1u);
+
+  if constexpr (kProfile) {
+    if (lane == 0) prof.stop();
+  }
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint32_t full_leader = cluster_map(smem_u32(&bar_full[0]), 0);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < tiles; t += npairs) {
+        int tm, tn;
+        tile_coord(t, args.tiles_m, args.tiles_n, args.group, &tm, &tn);
+        const int a_row = tm * kPairM + (int)rank * kCtaM;
+        const int b_row = tn * kPairN + (int)rank * kCtaN;
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if constexpr (kProfile) prof.start(kTagWaitMMA);
+          if (!wait_bounded(smem_u32(&bar_empty[stage]), phase ^ 1u, wctx, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          if constexpr (kProfile) { prof.stop(); prof.start(kTagIssueTMA); }
+          const uint32_t fb = full_leader + stage * 8u;
+          const uint32_t sa = smem_base + stage * kStageBytes;
+          mbar_arrive_expect_tx_cluster(fb, kStageBytes);
+          tma_load_2d_pair(sa, &tmap_a, kb * kBlockK, a_row, fb);
+          tma_load_2d_pair(sa + kStageBytesA, &tmap_b, kb * kBlockK, b_row, fb);
+          if constexpr (kProfile) prof.stop();
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if constexpr (kProfile) prof.flush();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = make_idesc_bf16_f32(kPairM, kPairN);
+      const uint32_t empty_self = cluster_map(smem_u32(&bar_empty[0]), 0);
+      const uint32_t empty_peer = cluster_map(smem_u32(&bar_empty[0]), 1);
+      const uint32_t accf_self = cluster_map(smem_u32(&bar_acc_full[0]), 0);
+      const uint32_t accf_peer = cluster_map(smem_u32(&bar_acc_full[0]), 1);
+      uint32_t stage = 0, phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < tiles; t += npairs, ++it) {
+        const uint32_t buf = it & 1, acc_phase = (it >> 1) & 1;
+        if constexpr (kProfile) prof.start(kTagWaitEpilogue);
+        if (!wait_bounded(smem_u32(&bar_acc_empty[buf]), acc_phase ^ 1u, wctx, kErrWaitAccEmpty))
+          break;
+        if constexpr (kProfile) prof.stop();
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + buf * kPairN;
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if constexpr (kProfile) prof.start(kTagWaitTMA);
+          if (!wait_bounded(smem_u32(&bar_full[stage]), phase, wctx, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          if constexpr (kProfile) { prof.stop(); prof.start(kTagIssueMMA); }
+          const uint32_t sa = smem_base + stage * kStageBytes;
+          const uint64_t adesc = make_sdesc_k128(sa);
+          const uint64_t bdesc = make_sdesc_k128(sa + kStageBytesA);
+#pragma unroll
+          for (int k = 0; k < kBlockK / kMmaK; ++k) {
+            // +32 B per K16 step inside the 128 B swizzled row (>>4 => +2)
+            umma_bf16_pair(d_tmem, adesc + 2ull * k, bdesc + 2ull * k, idesc,
+                           (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(empty_self + stage * 8u);
+          umma_commit_pair(empty_peer + stage * 8u);
+          if constexpr (kProfile) prof.stop();
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair(accf_self + buf * 8u);
+        umma_commit_pair(accf_peer + buf * 8u);
+      }
+      // Every MMA this thread issued must finish before TMEM is freed.
+      umma_commit_pair(cluster_map(smem_u32(&bar_drain), 0));
+      if (!mbar_try_wait(smem_u32(&bar_drain), 0))
+        wait_slow(smem_u32(&bar_drain), 0, wctx, kErrWaitDrain, false);
+    }
+    if constexpr (kProfile) {
+      if (lane == 0) prof.flush();
+    }
+    __syncwarp();
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int quarter = warp & 3;   // TMEM lanes this warp may read
+    const int ew = warp - 2;        // staging-buffer owner index
+    const uint32_t my_store = store_base + ew * 2 * kStoreBufBytes;
+    const uint32_t acc_empty_leader = cluster_map(smem_u32(&bar_acc_empty[0]), 0);
+    uint32_t nstore = 0;
+    int it = 0;
+    for (int t = pair; t < tiles; t += npairs, ++it) {
+      int tm, tn;
+      tile_coord(t, args.tiles_m, args.tiles_n, args.group, &tm, &tn);
+      const uint32_t buf = it & 1, acc_phase = (it >> 1) & 1;
+      if constexpr (kProfile) {
+        if (lane == 0) prof.start(kTagWaitMainloop);
+      }
+      // Lane 0 waits and the verdict is broadcast, so the warp stays converged
+      // for the warp-collective tcgen05.ld below.
+      int ok = 0;
+      if (lane == 0) ok = wait_bounded(smem_u32(&bar_acc_full[buf]), acc_phase, wctx, kErrWaitAccFull);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after_sync();
+      if constexpr (kProfile) {
+        if (lane == 0) { prof.stop(); prof.start(kTagEpilogue); }
+      }
+      const uint32_t tbase = tmem_base + buf * kPairN + ((uint32_t)(quarter * 32) << 16);
+      const int row0 = tm * kPairM + (int)rank * kCtaM + quarter * 32;
+      const int col0 = tn * kPairN;
+#pragma unroll 1
+      for (int c = 0; c < kPairN / kStoreCols; ++c) {
+        uint32_t v0[32], v1[32];
+        tmem_ld_32x32b_x32(tbase + c * kStoreCols, v0);
+        tmem_ld_32x32b_x32(tbase + c * kStoreCols + 32, v1);
+        tmem_wait_ld();
+        if (c == kPairN / kStoreCols - 1) {
+          // All of this buffer is in registers: hand TMEM back to the MMA.
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(acc_empty_leader + buf * 8u);
+        }
+        const uint32_t sb = my_store + (nstore & 1u) * kStoreBufBytes;
+        if (lane == 0) bulk_wait_group_read<1>();  // the store that last used sb has read it
+        __syncwarp();
+        // Row `lane` of the 32x64 box: 8 chunks of 16 B, chunk j stored at
+        // position j ^ (row % 8) -- the TMA 128 B swizzle pattern.
+        const uint32_t row_addr = sb + lane * 128u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          st_shared_v4(row_addr + ((uint32_t)(j ^ (lane & 7)) << 4),
+                       pack_bf16x2(v0[8 * j + 0], v0[8 * j + 1]),
+                       pack_bf16x2(v0[8 * j + 2], v0[8 * j + 3]),
+                       pack_bf16x2(v0[8 * j + 4], v0[8 * j + 5]),
+                       pack_bf16x2(v0[8 * j + 6], v0[8 * j + 7]));
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          st_shared_v4(row_addr + ((uint32_t)((j + 4) ^ (lane & 7)) << 4),
+                       pack_bf16x2(v1[8 * j + 0], v1[8 * j + 1]),
+                       pack_bf16x2(v1[8 * j + 2], v1[8 * j + 3]),
+                       pack_bf16x2(v1[8 * j + 4], v1[8 * j + 5]),
+                       pack_bf16x2(v1[8 * j + 6], v1[8 * j + 7]));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_c, sb, col0 + c * kStoreCols, row0);
+          bulk_commit_group();
+        }
+        ++nstore;
+      }
+      if constexpr (kProfile) {
+        if (lane == 0) prof.stop();
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    if constexpr (kProfile) {
+      if (lane == 0) prof.flush();
+    }
+    __syncwarp();
+  }
+
+  // ------------------------------------------------------------- teardown
+  tc_fence_before_sync();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+  cluster_sync_all();
+}
+
+// Self-test of the bounded wait: one CTA pair waits on a barrier that nothing
+// ever arrives on.  The wait must give up after timeout_ns, record
+// kErrWaitProbe in *status and return; nothing faults or hangs.
+__global__ void __cluster_dims__(2, 1, 1) wait_probe_kernel(int* status,
+                                                            unsigned long long timeout_ns) {
+  __shared__ alignas(8) uint64_t bar;
+  __shared__ uint32_t abort_word;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_word = 0;
+    fence_mbar_init_cluster();
+  }
+  cluster_sync_all();
+  if (threadIdx.x == 0 && cluster_ctarank() == 0) {
+    WaitCtx w;
+    w.status = status;
+    w.timeout_ns = timeout_ns;
+    w.abort_local = smem_u32(&abort_word);
+    w.abort_peer = cluster_map(smem_u32(&abort_word), 1);
+    wait_bounded(smem_u32(&bar), 0, w, kErrWaitProbe);
+  }
+  cluster_sync_all();
+}
+
+}  // namespace b200

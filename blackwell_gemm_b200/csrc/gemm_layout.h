@@ -1,0 +1,93 @@
+// Host/device shared layout rules of the sm_100a BF16 GEMM: the tile
+// geometry, the tcgen05 instruction and shared-memory descriptors, and the
+// persistent tile rasteriser.  Everything here is plain integer arithmetic so
+// the CPU tests can check it through the C-ABI without a GPU.
+//
+// Geometry (one 2-CTA cluster = one "pair"):
+//   pair tile        256 (M) x 256 (N), K stepped in blocks of 64
+//   per CTA          128 rows of A and 128 rows of B (its half of the N tile)
+//   MMA              tcgen05.mma.cta_group::2.kind::f16, M=256 N=256 K=16
+//   accumulator      fp32 in TMEM, 128 lanes x 256 columns per CTA, two
+//                    buffers (512 columns) so the epilogue of tile i
+//                    overlaps the main loop of tile i+1
+// The reference computes the same 256x256 cluster tile with BK=64
+// (kernel_v8.cu:775-833, launch_matmul_v8<128, 256, 64>).
+#pragma once
+#include <stdint.h>
+
+#if defined(__CUDACC__)
+#define B200_HD __host__ __device__ __forceinline__
+#else
+#define B200_HD static inline
+#endif
+
+namespace b200 {
+
+constexpr int kPairM = 256;        // rows of C per pair tile
+constexpr int kPairN = 256;        // columns of C per pair tile
+constexpr int kCtaM = 128;         // rows of A (and of C) owned by one CTA
+constexpr int kCtaN = 128;         // rows of B loaded by one CTA
+constexpr int kBlockK = 64;        // K elements per pipeline stage (= one 128 B swizzle row)
+constexpr int kMmaK = 16;          // K per tcgen05.mma kind::f16
+constexpr int kStages = 6;         // shared-memory ring depth
+constexpr int kAccBufs = 2;        // TMEM accumulator buffers
+constexpr int kTmemCols = kAccBufs * kPairN;   // 512 = the whole TMEM of an SM
+constexpr int kStoreCols = 64;     // epilogue chunk width (one 128 B swizzle row of bf16)
+constexpr int kEpiWarps = 4;       // epilogue warps (one per TMEM lane quarter)
+constexpr int kWarps = 2 + kEpiWarps;          // producer, MMA, 4 x epilogue
+constexpr int kThreads = kWarps * 32;
+
+constexpr int kStageBytesA = kCtaM * kBlockK * 2;          // 16 KiB
+constexpr int kStageBytesB = kCtaN * kBlockK * 2;          // 16 KiB
+constexpr int kStageBytes = kStageBytesA + kStageBytesB;   // 32 KiB per CTA per stage
+constexpr int kStoreBufBytes = 32 * kStoreCols * 2;        // 4 KiB: 32 rows x 64 columns
+constexpr int kStoreBytes = kEpiWarps * 2 * kStoreBufBytes; // 2 buffers per epilogue warp
+constexpr int kSmemBytes = kStages * kStageBytes + kStoreBytes + 1024;  // +1024 for 1 KiB alignment
+
+// ---------------------------------------------------------------------------
+// tcgen05 instruction descriptor for kind::f16 (PTX ISA "Instruction
+// descriptor" table): bits 4-5 D format (1 = f32), 7-9 A format (1 = bf16),
+// 10-12 B format (1 = bf16), 15/16 A/B major (0 = K-major), 17-22 N>>3,
+// 24-28 M>>4.  The reference packs the same fields (kernel_v8.cu:450-455).
+B200_HD uint32_t make_idesc_bf16_f32(int mma_m, int mma_n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) |
+         ((uint32_t)(mma_n >> 3) << 17) | ((uint32_t)(mma_m >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile written by TMA
+// with 128 B swizzling: rows of 128 B, 8-row swizzle atoms of 1024 B.
+//   bits  0-13 start address >> 4
+//   bits 16-29 leading byte offset >> 4 (unused for swizzled K-major: 0)
+//   bits 32-45 stride byte offset >> 4 (1024 B between 8-row groups)
+//   bits 46-47 descriptor version (1 on sm_100)
+//   bits 49-51 base offset (0: atoms are 1024 B aligned)
+//   bits 61-63 layout (2 = 128 B swizzle)
+// Same encoding as the reference's make_smem_desc (kernel_v1.cu:159-164).
+B200_HD uint64_t make_sdesc_k128(uint32_t smem_addr) {
+  return (uint64_t)((smem_addr & 0x3FFFFu) >> 4) |
+         ((uint64_t)(1024u >> 4) << 32) |
+         (1ull << 46) |
+         (2ull << 61);
+}
+
+// ---------------------------------------------------------------------------
+// Persistent tile rasteriser.  Pair tiles are numbered 0..tiles-1 and pair p
+// of P processes tiles p, p+P, p+2P, ...; consecutive numbers are therefore
+// in flight at the same time.  Numbers walk down a band of `group` tile-rows
+// before moving one tile-column right, so the ~74 tiles in flight touch about
+// group + 74/group distinct 256-row blocks of A and B instead of 2*74: that
+// is what keeps the working set of one wave inside the 126 MB L2.  The
+// reference instead deals a Hilbert curve over the tile grid
+// (kernel_v8.cu:338-358,796-820); both are permutations of the grid.
+B200_HD void tile_coord(int t, int tiles_m, int tiles_n, int group, int* tm, int* tn) {
+  const int band_tiles = group * tiles_n;
+  const int band = t / band_tiles;
+  const int first_m = band * group;
+  int rows = tiles_m - first_m;
+  if (rows > group) rows = group;
+  const int r = t - band * band_tiles;
+  *tm = first_m + r % rows;
+  *tn = r / rows;
+}
+
+}  // namespace b200

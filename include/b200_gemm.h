@@ -1,0 +1,95 @@
+/* C ABI of the sm_100a BF16 GEMM (libb200gemm.so).
+ *
+ * The reference exposes its GEMM as
+ *     void matmul_vN(const nv_bfloat16 *A, const nv_bfloat16 *B,
+ *                    nv_bfloat16 *C, int M, int N, int K);
+ * (src/matmul.cpp:4-23, bodies e.g. src/kernels/kernel_v8.cu:830-833) and
+ *     void profile_matmul_vN(..., int64_t *profiler_ptr, int num_entries);
+ * (src/matmul.cpp:16-23, src/kernels/kernel_v8.cu:835-839).  The entry points
+ * below replace those: same operand meaning (C = A * B^T, A is M x K
+ * row-major, B is N x K row-major -- the reference's "(K,N) view of an N x K
+ * buffer" -- and C is M x N row-major, bf16 in/out, fp32 accumulation), plus
+ * explicit leading dimensions, an explicit CUDA stream (0 = legacy default
+ * stream, where the reference launches) and a status code instead of silent
+ * garbage on unsupported input.
+ *
+ * All pointers are device pointers.  Calls are asynchronous on `stream`.
+ * Plain C types only; no torch types cross this boundary.
+ */
+#ifndef B200_GEMM_H_
+#define B200_GEMM_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by every entry point. */
+#define B200_OK 0
+#define B200_ERR_INVALID_ARGUMENT 1 /* null pointer, negative size, ld < width */
+#define B200_ERR_ALIGNMENT 2        /* pointer or leading dimension not 16 B aligned */
+#define B200_ERR_UNSUPPORTED_DEVICE 3 /* current device is not sm_100 */
+#define B200_ERR_TENSOR_MAP 4       /* cuTensorMapEncodeTiled rejected the operand */
+#define B200_ERR_LAUNCH 5           /* CUDA error at or before the launch */
+#define B200_ERR_DEVICE_TIMEOUT 6   /* a kernel pipeline wait ran out (see device_status) */
+#define B200_ERR_TOO_LARGE 7        /* a size exceeds what the entry point supports */
+
+/* C = A * B^T, bf16 in and out, fp32 accumulation.
+ * A: M x K, row stride lda elements.  B: N x K, row stride ldb.  C: M x N,
+ * row stride ldc.  Requirements: lda >= K, ldb >= K, ldc >= N; lda, ldb, ldc
+ * multiples of 8 and A, B, C 16-byte aligned (TMA); M, N, K >= 0.  M == 0 or
+ * N == 0 is a no-op; K == 0 writes zeros.  Any other M, N, K is supported
+ * (ragged edges are handled by the TMA bounds).
+ * Replaces matmul_v1_2d ... matmul_v8 (src/matmul.cpp:4-13). */
+int b200_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
+                   int ldc, void* stream);
+
+/* Same GEMM with the intra-kernel profiler on.  `profiler` is a device int64
+ * buffer of rows x (1 + 4 * num_entries) entries, rows from
+ * b200_gemm_profile_rows; row r = block * 6 + warp holds
+ * [count, (smid, tag, start_ns, duration_ns) x count].  Writes past a row's
+ * capacity are dropped.
+ * Replaces profile_matmul_v5 ... profile_matmul_v8 (src/matmul.cpp:16-23). */
+int b200_gemm_bf16_profile(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                           int ldb, int ldc, int64_t* profiler, int num_entries, void* stream);
+
+/* Rows the profiler buffer needs for an M x N x K launch on the current
+ * device (grid size x warps per CTA).  No reference counterpart: the
+ * reference sizes this buffer by hand and under-sizes it for v8
+ * (src/bench_core.py:459-464 vs src/kernels/kernel_v8.cu:416). */
+int b200_gemm_profile_rows(int M, int N, int K, int* rows);
+
+/* Reads (and if `clear`, resets) the device error word of the current device
+ * that the kernels write when a pipeline wait runs out.  Synchronises the
+ * device.  *status_out = 0 when no wait has run out.  No reference
+ * counterpart (the reference's waits never give up, kernel_v8.cu:60-76). */
+int b200_gemm_device_status(int clear, int* status_out);
+
+/* Upper bound, in nanoseconds, on any single pipeline wait inside the GEMM
+ * kernels of this process (default 2 s).  No reference counterpart. */
+int b200_gemm_set_wait_timeout_ns(unsigned long long timeout_ns);
+
+/* Launches a self-test kernel whose only wait is on a barrier nothing
+ * releases, bounded by timeout_ns; the kernel records the timeout in the
+ * device error word and returns.  Used by the failure-detection tests.  No
+ * reference counterpart. */
+int b200_gemm_wait_probe(unsigned long long timeout_ns, void* stream);
+
+/* Short text for a status code. */
+const char* b200_gemm_status_string(int status);
+
+/* Host-side layout rules, exported so they can be checked without a GPU. */
+void b200_gemm_tile_coord(int t, int tiles_m, int tiles_n, int group, int* tm, int* tn);
+uint32_t b200_gemm_idesc(int mma_m, int mma_n);
+uint64_t b200_gemm_smem_desc(uint32_t smem_addr);
+/* Launch geometry the GEMM would use: pair tiles, grid CTAs (0 if no
+ * device), dynamic shared memory bytes and threads per CTA. */
+int b200_gemm_launch_shape(int M, int N, int K, int* tiles, int* grid, int* smem_bytes,
+                           int* threads);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_GEMM_H_ */

@@ -1,0 +1,38 @@
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100) GPU")
+
+
+def _has_b200() -> bool:
+    try:
+        import torch
+        return torch.cuda.is_available() and torch.cuda.get_device_capability(0) == (10, 0)
+    except Exception:
+        return False
+
+
+HAS_B200 = _has_b200()
+
+
+def pytest_collection_modifyitems(config, items):
+    if HAS_B200:
+        return
+    skip = pytest.mark.skip(reason="no sm_100 GPU in this environment")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)
+
+
+@pytest.fixture(scope="session")
+def repo_root() -> Path:
+    return ROOT

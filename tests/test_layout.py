@@ -1,0 +1,101 @@
+"""Host-side layout rules of the kernel, checked through the C ABI (no GPU).
+
+Descriptor fields are checked against the bit positions of the PTX ISA
+tables for tcgen05 (instruction descriptor of kind::f16, shared-memory matrix
+descriptor); the rasteriser is checked to visit every tile exactly once.
+"""
+import pytest
+
+from blackwell_gemm_b200 import capi
+
+
+def bits(x, lo, hi):
+    """Field [lo, hi) of x."""
+    return (x >> lo) & ((1 << (hi - lo)) - 1)
+
+
+@pytest.mark.parametrize("m,n", [(256, 256), (128, 256), (256, 128), (128, 64), (64, 8)])
+def test_instruction_descriptor_fields(m, n):
+    d = capi.idesc(m, n)
+    assert bits(d, 0, 4) == 0          # dense, no saturate
+    assert bits(d, 4, 6) == 1          # D = f32
+    assert bits(d, 7, 10) == 1         # A = bf16
+    assert bits(d, 10, 13) == 1        # B = bf16
+    assert bits(d, 13, 15) == 0        # no negation
+    assert bits(d, 15, 17) == 0        # A and B K-major
+    assert bits(d, 17, 23) == n >> 3
+    assert bits(d, 23, 24) == 0
+    assert bits(d, 24, 29) == m >> 4
+    assert bits(d, 29, 32) == 0
+
+
+def test_instruction_descriptor_matches_reference_packing():
+    # kernel_v8.cu:450-455 packs (1<<4)|(1<<7)|(1<<10)|(BN>>3<<17)|((2*BM)>>4<<24)
+    ref = (1 << 4) | (1 << 7) | (1 << 10) | ((256 >> 3) << 17) | ((2 * 128) >> 4 << 24)
+    assert capi.idesc(256, 256) == ref
+
+
+@pytest.mark.parametrize("addr", [0, 1024, 0x8000, 0x30000, 0x37C00, 1024 + 32, 1024 + 96])
+def test_smem_descriptor_fields(addr):
+    d = capi.smem_desc(addr)
+    assert bits(d, 0, 14) == (addr & 0x3FFFF) >> 4    # start address >> 4
+    assert bits(d, 16, 30) == 0                       # LBO unused (swizzled K-major)
+    assert bits(d, 32, 46) == 1024 >> 4               # SBO: 8 rows x 128 B
+    assert bits(d, 46, 48) == 1                       # sm_100 descriptor version
+    assert bits(d, 49, 52) == 0                       # base offset
+    assert bits(d, 52, 53) == 0                       # LBO mode
+    assert bits(d, 61, 64) == 2                       # 128 B swizzle
+
+
+def test_smem_descriptor_k_advance_is_plus_two():
+    # The kernel adds 2 (= 32 B >> 4) per K16 step to the descriptor itself.
+    for base in (0, 1024, 0x20000):
+        for k in range(4):
+            assert capi.smem_desc(base + 32 * k) == capi.smem_desc(base) + 2 * k
+
+
+@pytest.mark.parametrize("tm,tn,group", [(32, 32, 8), (1, 1, 8), (4, 64, 8), (33, 7, 8),
+                                          (5, 5, 16), (112, 24, 8), (32, 32, 1), (3, 9, 2)])
+def test_raster_is_a_permutation(tm, tn, group):
+    seen = set()
+    for t in range(tm * tn):
+        m, n = capi.tile_coord(t, tm, tn, group)
+        assert 0 <= m < tm and 0 <= n < tn
+        seen.add((m, n))
+    assert len(seen) == tm * tn
+
+
+def test_raster_bands_keep_wave_working_set_small():
+    # 74 consecutive tiles (one wave of pairs on 148 SMs) at 8192^3 touch at
+    # most ~group + 74/group distinct A row blocks + B column blocks.
+    tm = tn = 32
+    for start in range(0, tm * tn - 74, 37):
+        ms, ns = set(), set()
+        for t in range(start, start + 74):
+            m, n = capi.tile_coord(t, tm, tn, 8)
+            ms.add(m)
+            ns.add(n)
+        assert len(ms) + len(ns) <= 8 + 8 + 11
+
+
+def test_persistent_assignment_covers_all_tiles_once():
+    tiles, pairs = 1024, 74
+    owner = {}
+    for p in range(pairs):
+        for t in range(p, tiles, pairs):
+            assert t not in owner
+            owner[t] = p
+    assert len(owner) == tiles
+    loads = [len(range(p, tiles, pairs)) for p in range(pairs)]
+    assert max(loads) - min(loads) <= 1
+
+
+def test_launch_shape_without_gpu():
+    s = capi.launch_shape(8192, 8192, 8192)
+    assert s["tiles"] == 32 * 32
+    assert s["threads"] == 192
+    assert s["smem_bytes"] <= 227 * 1024
+    s = capi.launch_shape(16, 8192, 8192)
+    assert s["tiles"] == 32
+    s = capi.launch_shape(300, 520, 200)
+    assert s["tiles"] == 2 * 3
