@@ -1,0 +1,460 @@
+"""Benchmark of the B200 BF16 GEMM: cold-L2 TFLOP/s at 8192^3 per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
+
+One step = one C = A * B^T of the hot path on one batch of synthetic input.
+Each rank owns an 8192-row block of A and a replicated 8192 x 8192 B (the
+row-sharded configuration: M = 8192 * N in total, no collective), so per-GPU
+work is fixed as N grows ("scaling": "weak").  At N = 1 this is the 8192^3
+headline shape.  Operands are seeded N(0, 1) bf16, generated on the device.
+
+Timing follows the reference harness (src/bench_core.py:47-69): a 256 MB
+buffer is written before every step so L2 is cold, and each GEMM is bracketed
+by CUDA events on the launching stream; the K timed steps sit between a
+barrier + synchronize on both sides, and the per-rank GEMM time is maxed over
+ranks.  Rank 0 prints one JSON line.
+
+Extra measurements in the same line: e2e (the same GEMM through the C ABI
+with pinned host buffers, copies inside the timed region), the roofline of
+the kernel against the measured bf16 peak, SM clocks sampled during the timed
+region, same-process baselines (cuBLAS and the reference's own v8 kernel) and
+the CPU oracle timed on the host's cores on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+M_PER_GPU, N_DIM, K_DIM = 8192, 8192, 8192
+FLUSH_BYTES = 256 * 1024 * 1024
+FALLBACK_BF16_TFLOPS = 1590.0      # earlier measurement on this pool (burst)
+
+
+# --------------------------------------------------------------- utilities
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return d, "measured"
+        except Exception:
+            pass
+    return {"bf16_tflops": FALLBACK_BF16_TFLOPS, "hbm_gbs": 6650.0}, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per launch of the kernel at the bench shape, from the
+    committed ncu summary (profiles/*.md, line 'traffic_bytes_per_launch: N')."""
+    for p in sorted((ROOT / "profiles").glob("gemm_bf16_pair*8192*.md")):
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", p.read_text())
+        if m:
+            return int(m.group(1)), p.name
+    return None, None
+
+
+def pci_bus_string(device: int) -> str:
+    """NVML bus id "DDDDDDDD:BB:DD.0" of a CUDA device (torch reports the
+    domain, bus and device numbers as integers; NVML's device order differs
+    from CUDA's under CUDA_VISIBLE_DEVICES, so the handle is looked up by bus)."""
+    p = torch.cuda.get_device_properties(device)
+    dom, bus, dev = p.pci_domain_id, p.pci_bus_id, p.pci_device_id
+    if not all(isinstance(v, int) for v in (dom, bus, dev)):
+        raise TypeError("unexpected PCI id types from torch")
+    return f"{dom:08X}:{bus:02X}:{dev:02X}.0"
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons of one GPU through NVML."""
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, device: int, period_s: float = 0.01):
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self.period, self._stop, self._th, self.err = period_s, threading.Event(), None, None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(pci_bus_string(device).encode())
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # NVML missing: report it, do not fail the bench
+            self.nv, self.err = None, repr(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= int(self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+            except Exception as e:
+                self.err = repr(e)
+                return
+            time.sleep(self.period)
+
+    def start(self):
+        if self.nv:
+            self._th = threading.Thread(target=self._run, daemon=True)
+            self._th.start()
+
+    def stop(self):
+        if self._th:
+            self._stop.set()
+            self._th.join()
+
+    def report(self):
+        names = [n for b, n in self.REASONS.items() if self.reasons & b]
+        out = {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+               "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+        if self.err:
+            out["error"] = self.err
+        return out
+
+
+def cold_l2_loop(fn, steps, stream, flush):
+    """Per step: write the flush buffer, then time fn() with events."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record(stream)
+        fn()
+        ends[i].record(stream)
+    return starts, ends
+
+
+def time_cold(fn, steps, warmup, stream, flush):
+    for _ in range(warmup):
+        flush.zero_()
+        fn()
+    torch.cuda.synchronize()
+    s, e = cold_l2_loop(fn, steps, stream, flush)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in zip(s, e)]
+
+
+# ------------------------------------------------------------------- arms
+def gemm_ours(A, Bt, C, stream):
+    """The product call the bench times: the C ABI on device pointers."""
+    from blackwell_gemm_b200 import capi
+    M, K = A.shape
+    N = Bt.shape[0]
+    st = capi.gemm_bf16(A.data_ptr(), Bt.data_ptr(), C.data_ptr(), M, N, K, K, K, N,
+                        stream.cuda_stream)
+    if st != 0:
+        raise RuntimeError(f"b200_gemm_bf16 failed: {capi.status_string(st)}")
+
+
+def gemm_reference(A, Bt, C, stream):
+    """The reference's own matmul_v8, through its launcher (legacy stream)."""
+    import oracle
+    M, K = A.shape
+    N = Bt.shape[0]
+    oracle.ref_gemm("v8", A.data_ptr(), Bt.data_ptr(), C.data_ptr(), M, N, K)
+
+
+def parity_sample(C, A, Bt, nrows=256, seed=1):
+    from blackwell_gemm_b200 import parity
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    rows = torch.randperm(A.shape[0], generator=g)[:nrows].to(A.device)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        R = A.index_select(0, rows).float() @ Bt.float().T
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    m = parity.metrics(C, R, A, Bt, rows=rows)
+    return {"max_scaled": m["max_scaled"], "rel_fro": m["rel_fro"], "pass": parity.passes(m),
+            "rows_checked": nrows, "against": "fp32 GEMM of the same bf16 inputs (GPU, no TF32)"}
+
+
+def e2e_measure(gemm, A, Bt, stream, steps=8, warmup=2):
+    """Same GEMM with host buffers: H2D of A and B from pinned memory, the
+    call, D2H of C, all inside the timed region, one stream."""
+    M, K = A.shape
+    N = Bt.shape[0]
+    hA = A.cpu().pin_memory()
+    hB = Bt.cpu().pin_memory()
+    hC = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+    dA = torch.empty_like(A)
+    dB = torch.empty_like(Bt)
+    dC = torch.empty(M, N, dtype=torch.bfloat16, device=A.device)
+
+    def step():
+        dA.copy_(hA, non_blocking=True)
+        dB.copy_(hB, non_blocking=True)
+        gemm(dA, dB, dC, stream)
+        hC.copy_(dC, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(steps):
+            step()
+        e.record(stream)
+        torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    return ms, 2 * (M * K + N * K), 2 * M * N
+
+
+def cpu_baseline(Bt, rows=256):
+    """CPU oracle (C restatement, all host threads) on `rows` rows of A against
+    the full B; TFLOP/s extrapolates linearly in M."""
+    import numpy as np
+    import oracle
+    B_u16 = Bt.cpu().view(torch.int16).numpy().view(np.uint16)
+    rng = np.random.default_rng(0)
+    A_u16 = oracle.round_bf16(rng.standard_normal((rows, Bt.shape[1]), dtype=np.float32))
+    threads = oracle.default_threads()
+    t0 = time.perf_counter()
+    oracle.gemm_f32(A_u16, B_u16, nthreads=threads)
+    dt = time.perf_counter() - t0
+    flops = 2 * rows * Bt.shape[0] * Bt.shape[1]
+    out = {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+           "sample": f"{rows} x {Bt.shape[0]} x {Bt.shape[1]} (rows of A against the full B); "
+                     f"{dt:.2f} s; rate scales linearly in M",
+           "seconds": dt}
+    # torch's CPU bf16 matmul on the same sample (the configuration's third baseline)
+    a = torch.from_numpy(A_u16.view(np.int16)).view(torch.bfloat16)
+    b = Bt.cpu()
+    t0 = time.perf_counter()
+    torch.matmul(a, b.T)
+    dt2 = time.perf_counter() - t0
+    out["torch_cpu_bf16"] = {"value": flops / dt2 / 1e12, "unit": "TFLOP/s",
+                             "threads": torch.get_num_threads(), "seconds": dt2}
+    return out
+
+
+# ------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip e2e, baselines and the CPU sample (timing only)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; using {world}",
+              file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    if args.impl == "reference":
+        return run_reference(args, world, rank, dev)
+
+    import torch.distributed as dist
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    import blackwell_gemm_b200  # noqa: F401  (loads the native library; fails loudly)
+    from blackwell_gemm_b200.workloads import make_operands
+
+    M, N, K = M_PER_GPU, N_DIM, K_DIM
+    A, _ = make_operands(M, 8, K, seed=1000 + rank, device=dev)        # this rank's rows
+    _, Bt = make_operands(8, N, K, seed=0, device=dev)                 # replicated B
+    C = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    gemm_ours(A, Bt, C, stream)
+    torch.cuda.synchronize()
+    par = parity_sample(C, A, Bt)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        gemm_ours(A, Bt, C, stream)
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    region_s = torch.cuda.Event(enable_timing=True)
+    region_e = torch.cuda.Event(enable_timing=True)
+    region_s.record(stream)
+    starts, ends = cold_l2_loop(lambda: gemm_ours(A, Bt, C, stream), args.steps, stream, flush)
+    region_e.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks.stop()
+    launch_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    gemm_ms_total = sum(launch_ms)
+    region_ms = region_s.elapsed_time(region_e)
+    t = torch.tensor([gemm_ms_total, region_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    gemm_ms_max, region_ms_max = float(t[0]), float(t[1])
+
+    flops_step = 2 * M * N * K
+    value = flops_step * world * args.steps / (gemm_ms_max * 1e-3) / 1e12
+    ms_per_step = gemm_ms_max / args.steps
+
+    # e2e through the C ABI with host buffers, every rank
+    e2e = None
+    if not args.no_extras:
+        e_ms, h2d, d2h = e2e_measure(gemm_ours, A, Bt, stream)
+        et = torch.tensor([e_ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e2e = {"value": flops_step * world / (float(et[0]) * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+               "ms_per_step": float(et[0]),
+               "path": "capi.gemm_bf16 (b200_gemm_bf16) with pinned host A, B and C"}
+
+    peaks, peak_src = measured_peaks()
+    traffic, traffic_src = profiled_traffic()
+    mean_launch_ms = statistics.mean(launch_ms)
+    achieved = flops_step / (mean_launch_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                "traffic": traffic,
+                "peak_source": f"{peak_src} (bf16 burst: kernel timed alone)",
+                "algorithmic_flops_per_launch": flops_step,
+                "algorithmic_bytes_per_launch": 2 * (M * K + N * K + M * N),
+                "traffic_source": traffic_src}
+
+    extras = {}
+    if rank == 0 and world == 1 and not args.no_extras:
+        ref_ms = None
+        try:
+            import oracle
+            Cr = torch.empty_like(C)
+            if oracle.ref_supports("v8", M, N, K):
+                ref_ms = statistics.median(time_cold(lambda: gemm_reference(A, Bt, Cr, stream),
+                                                     50, 10, stream, flush))
+        except Exception as e:  # the reference build may be absent
+            extras["reference_v8_error"] = repr(e)
+        cub_ms = statistics.median(time_cold(lambda: torch.matmul(A, Bt.T), 50, 10, stream, flush))
+        ours_med = statistics.median(launch_ms)
+        extras["baselines"] = {
+            "ours_median_tflops": flops_step / (ours_med * 1e-3) / 1e12,
+            "cublas_median_tflops": flops_step / (cub_ms * 1e-3) / 1e12,
+            "reference_v8_median_tflops": (flops_step / (ref_ms * 1e-3) / 1e12) if ref_ms else None,
+            "method": "median of 50 cold-L2 launches each, same process and inputs "
+                      "(src/bench_core.py:47-69 method)"}
+        extras["cpu_baseline"] = cpu_baseline(Bt)
+
+    if rank == 0:
+        line = {
+            "metric": "BF16 GEMM TFLOP/s (cold-L2) at 8192^3 per GPU",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "bf16 GEMM C = A B^T, 8192 x 8192 x 8192 per GPU "
+                                   "(rows of A sharded, B replicated, no collective)",
+                       "M": M * world, "N": N, "K": K, "m_per_gpu": M,
+                       "inputs": "A, B iid N(0,1) bf16, seeded, resident in HBM",
+                       "l2": "flushed: 256 MB written before every step, outside the GEMM events",
+                       "parallelism": f"m-shard{world}"},
+            "timed_region_ms": region_ms_max,
+            "gpu_launches": args.steps,
+            "roofline": roofline,
+            "e2e": e2e,
+            "clocks": clocks.report(),
+            "parity": par,
+            "impl": "ours",
+        }
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args, world, rank, dev):
+    """The reference's own implementation of the path: its matmul_v8 kernel
+    (src/kernels/kernel_v8.cu:830-833), built from its sources into
+    oracle/_ref by oracle/build.py and called through its launcher.  The
+    reference has no CPU implementation; this GPU kernel is it.  Rank 0 alone
+    runs (single-GPU reference); other ranks exit without work."""
+    if rank != 0:
+        return
+    try:
+        import oracle
+        oracle.ref_lib()
+    except Exception as e:
+        print(json.dumps({"impl": "reference",
+                          "unavailable": f"reference build oracle/_ref missing: {e}"}))
+        return
+    from blackwell_gemm_b200.workloads import make_operands
+    M, N, K = M_PER_GPU, N_DIM, K_DIM
+    A, _ = make_operands(M, 8, K, seed=1000, device=dev)
+    _, Bt = make_operands(8, N, K, seed=0, device=dev)
+    C = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    gemm_reference(A, Bt, C, stream)
+    torch.cuda.synchronize()
+    par = parity_sample(C, A, Bt)
+    for _ in range(args.warmup):
+        flush.zero_()
+        gemm_reference(A, Bt, C, stream)
+    clocks = ClockSampler(dev.index)
+    torch.cuda.synchronize()
+    clocks.start()
+    starts, ends = cold_l2_loop(lambda: gemm_reference(A, Bt, C, stream), args.steps, stream,
+                                flush)
+    torch.cuda.synchronize()
+    clocks.stop()
+    launch_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    total = sum(launch_ms)
+    flops_step = 2 * M * N * K
+    value = flops_step * args.steps / (total * 1e-3) / 1e12
+    e_ms, h2d, d2h = e2e_measure(gemm_reference, A, Bt, stream)
+    line = {
+        "metric": "BF16 GEMM TFLOP/s (cold-L2) at 8192^3 per GPU",
+        "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "bf16 GEMM C = A B^T, 8192 x 8192 x 8192 per GPU "
+                               "(reference runs on rank 0 only)",
+                   "M": M, "N": N, "K": K,
+                   "l2": "flushed: 256 MB written before every step, outside the GEMM events",
+                   "parallelism": "single GPU"},
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": 0, "kind": "reference",
+                         "sample": "the reference's matmul_v8 GPU kernel on the full workload "
+                                   "(the reference has no CPU implementation of the path)"},
+        "e2e": {"value": flops_step / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e_ms,
+                "path": "reference matmul_v8 launcher with pinned host A, B and C"},
+        "gpu_launches": 0,
+        "clocks": clocks.report(),
+        "parity": par,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

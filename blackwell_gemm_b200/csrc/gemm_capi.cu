@@ -63,18 +63,36 @@ int env_int(const char* name, int fallback, int lo, int hi) {
   return (x < lo || x > hi) ? fallback : x;
 }
 
-// Band height (tile-rows) of the grouped raster; B200_GEMM_GROUP overrides.
+// Tuning knobs, process-wide: band height (tile-rows) of the grouped raster
+// and K slabs (64 elements each) per pipeline stage.  Initialised from
+// B200_GEMM_GROUP / B200_GEMM_SLABS, changeable through b200_gemm_set_tuning.
+std::atomic<int> g_group{-1};
+std::atomic<int> g_slabs{-1};
+
 int raster_group() {
-  static const int g = env_int("B200_GEMM_GROUP", 8, 1, 1 << 16);
+  int g = g_group.load();
+  if (g < 0) {
+    g = env_int("B200_GEMM_GROUP", 8, 1, 1 << 16);
+    g_group.store(g);
+  }
   return g;
 }
 
+int stage_slabs() {
+  int s = g_slabs.load();
+  if (s < 0) {
+    s = env_int("B200_GEMM_SLABS", 1, 1, 2);
+    g_slabs.store(s);
+  }
+  return s;
+}
+
 template <typename K>
-int max_active_pairs(K kernel, int sms, int* out) {
+int max_active_pairs(K kernel, int sms, int smem_bytes, int* out) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * sms, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.dynamicSmemBytes = smem_bytes;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
@@ -86,6 +104,13 @@ int max_active_pairs(K kernel, int sms, int* out) {
   if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) return B200_ERR_LAUNCH;
   *out = n;
   return B200_OK;
+}
+
+template <bool kProfile, int kSlabs>
+cudaError_t set_smem_limit() {
+  return cudaFuncSetAttribute(gemm_bf16_pair_kernel<kProfile, kSlabs>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              Pipe<kSlabs>::kSmemBytes);
 }
 
 int device_state(DeviceState** out) {
@@ -109,14 +134,13 @@ int device_state(DeviceState** out) {
     } else {
       d.sms = prop.multiProcessorCount;
       int st = B200_OK;
-      if (cudaFuncSetAttribute(gemm_bf16_pair_kernel<false>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-              cudaSuccess ||
-          cudaFuncSetAttribute(gemm_bf16_pair_kernel<true>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-              cudaSuccess)
+      if (set_smem_limit<false, 1>() != cudaSuccess || set_smem_limit<true, 1>() != cudaSuccess ||
+          set_smem_limit<false, 2>() != cudaSuccess || set_smem_limit<true, 2>() != cudaSuccess)
         st = B200_ERR_LAUNCH;
-      if (st == B200_OK) st = max_active_pairs(gemm_bf16_pair_kernel<false>, d.sms, &d.max_pairs);
+      // Every variant runs one CTA per SM, so one occupancy query sizes all.
+      if (st == B200_OK)
+        st = max_active_pairs(gemm_bf16_pair_kernel<false, 1>, d.sms, Pipe<1>::kSmemBytes,
+                              &d.max_pairs);
       if (st == B200_OK && d.max_pairs < 1) st = B200_ERR_LAUNCH;
       if (st == B200_OK) {
         if (cudaMalloc(&d.status, sizeof(int)) != cudaSuccess ||
@@ -134,6 +158,21 @@ int device_state(DeviceState** out) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// L2 promotion of the operand loads; B200_GEMM_L2_PROMO in {0, 64, 128, 256}
+// overrides (the reference exposes the same knob as GEMM_L2_A / GEMM_L2_B,
+// kernel_v8.cu:11-31).
+CUtensorMapL2promotion l2_promotion() {
+  static const CUtensorMapL2promotion p = []() {
+    switch (env_int("B200_GEMM_L2_PROMO", 256, 0, 256)) {
+      case 0: return CU_TENSOR_MAP_L2_PROMOTION_NONE;
+      case 64: return CU_TENSOR_MAP_L2_PROMOTION_L2_64B;
+      case 128: return CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
+      default: return CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
+    }
+  }();
+  return p;
+}
+
 int encode_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
               uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
   const cuuint64_t dims[2] = {inner, outer};
@@ -143,7 +182,7 @@ int encode_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer
   const CUresult r = encode_tiled()(
       map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      l2_promotion(), CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TENSOR_MAP;
 }
 
@@ -176,18 +215,20 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda
                : B200_ERR_LAUNCH;
   }
   CUtensorMap ta, tb, tc;
-  if (encode_2d(&ta, A, K, M, lda, kBlockK, kCtaM) != B200_OK ||
-      encode_2d(&tb, B, K, N, ldb, kBlockK, kCtaN) != B200_OK ||
+  if (encode_2d(&ta, A, K, M, lda, kSlabK, kCtaM) != B200_OK ||
+      encode_2d(&tb, B, K, N, ldb, kSlabK, kCtaN) != B200_OK ||
       encode_2d(&tc, C, N, M, ldc, kStoreCols, 32) != B200_OK)
     return B200_ERR_TENSOR_MAP;
 
+  const int slabs = stage_slabs();
+  const int bk = slabs * kSlabK;
   GemmArgs args;
   args.M = M;
   args.N = N;
   args.K = K;
   args.tiles_m = (M + kPairM - 1) / kPairM;
   args.tiles_n = (N + kPairN - 1) / kPairN;
-  args.k_blocks = (K + kBlockK - 1) / kBlockK;
+  args.k_blocks = (K + bk - 1) / bk;
   args.group = raster_group();
   args.status = d->status;
   args.timeout_ns = g_timeout_ns.load();
@@ -195,7 +236,12 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda
   args.prof_entries = prof_entries;
   const long long tiles = (long long)args.tiles_m * args.tiles_n;
   const int pairs = (int)(tiles < d->max_pairs ? tiles : d->max_pairs);
-  gemm_bf16_pair_kernel<kProfile><<<2 * pairs, kThreads, kSmemBytes, stream>>>(ta, tb, tc, args);
+  if (slabs == 2)
+    gemm_bf16_pair_kernel<kProfile, 2><<<2 * pairs, kThreads, Pipe<2>::kSmemBytes, stream>>>(
+        ta, tb, tc, args);
+  else
+    gemm_bf16_pair_kernel<kProfile, 1><<<2 * pairs, kThreads, Pipe<1>::kSmemBytes, stream>>>(
+        ta, tb, tc, args);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
 }
 
@@ -220,7 +266,7 @@ int b200_gemm_launch_shape(int M, int N, int K, int* tiles, int* grid, int* smem
   if (M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARGUMENT;
   const long long t = (long long)((M + kPairM - 1) / kPairM) * ((N + kPairN - 1) / kPairN);
   if (tiles) *tiles = (int)t;
-  if (smem_bytes) *smem_bytes = kSmemBytes;
+  if (smem_bytes) *smem_bytes = stage_slabs() == 2 ? Pipe<2>::kSmemBytes : Pipe<1>::kSmemBytes;
   if (threads) *threads = kThreads;
   if (grid) {
     *grid = 0;
@@ -252,6 +298,19 @@ int b200_gemm_device_status(int clear, int* status_out) {
   if (clear && v != 0 && cudaMemset(d->status, 0, sizeof(int)) != cudaSuccess)
     return B200_ERR_LAUNCH;
   *status_out = v;
+  return B200_OK;
+}
+
+int b200_gemm_set_tuning(int stage_slabs, int raster_group) {
+  if (stage_slabs < 0 || stage_slabs > 2 || raster_group < 0) return B200_ERR_INVALID_ARGUMENT;
+  if (stage_slabs > 0) g_slabs.store(stage_slabs);
+  if (raster_group > 0) g_group.store(raster_group);
+  return B200_OK;
+}
+
+int b200_gemm_get_tuning(int* stage_slabs_out, int* raster_group_out) {
+  if (stage_slabs_out) *stage_slabs_out = stage_slabs();
+  if (raster_group_out) *raster_group_out = raster_group();
   return B200_OK;
 }
 

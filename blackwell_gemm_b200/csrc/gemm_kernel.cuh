@@ -102,23 +102,27 @@ __device__ __forceinline__ uint32_t ld_volatile_shared(uint32_t addr) {
   return v;
 }
 
-// Wait for `parity` on a local mbarrier.  Gives up when the abort word is set
-// (another warp of the pair already gave up) or after timeout_ns; in the
-// latter case it records `code`, raises both CTAs' abort words and returns
-// false so the caller can leave its loop and reach the teardown.
+// Wait for `parity` on a local mbarrier.  Each poll may sleep up to
+// kPollSuspendNs (it returns as soon as the phase completes).  Gives up when
+// the abort word is set (another warp of the pair already gave up) or once
+// timeout_ns has passed; in the latter case it records `code`, raises both
+// CTAs' abort words and returns false so the caller can leave its loop and
+// reach the teardown.  The bound is timeout_ns plus at most one burst of
+// polls.
 __device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, const WaitCtx& w, int code,
                                        bool honour_abort) {
   const unsigned long long t0 = globaltimer_ns();
-  for (uint32_t spin = 1;; ++spin) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((spin & 15u) == 0) {
-      if (honour_abort && ld_volatile_shared(w.abort_local) != 0) return false;
-      if (globaltimer_ns() - t0 > w.timeout_ns) {
-        atomicCAS(w.status, 0, code);
-        asm volatile("st.volatile.shared.u32 [%0], %1;" :: "r"(w.abort_local), "r"(1u) : "memory");
-        st_cluster_u32(w.abort_peer, 1u);
-        return false;
-      }
+  for (;;) {
+    // Poll in bursts; the abort word and the clock are read once per burst.
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (honour_abort && ld_volatile_shared(w.abort_local) != 0) return false;
+    if (globaltimer_ns() - t0 > w.timeout_ns) {
+      atomicCAS(w.status, 0, code);
+      asm volatile("st.volatile.shared.u32 [%0], %1;" :: "r"(w.abort_local), "r"(1u) : "memory");
+      st_cluster_u32(w.abort_peer, 1u);
+      return false;
     }
   }
 }
@@ -134,12 +138,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <bool kProfile>
+template <bool kProfile, int kSlabs>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_c,
                       const GemmArgs args) {
+  using P = Pipe<kSlabs>;
+  constexpr int kStages = P::kStages;
   extern __shared__ uint8_t smem_raw[];
   __shared__ alignas(8) uint64_t bar_full[kStages];
   __shared__ alignas(8) uint64_t bar_empty[kStages];
@@ -158,7 +164,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
 
   // 1 KiB aligned start: the 128 B swizzle atoms (8 rows x 128 B) must be.
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const uint32_t store_base = smem_base + kStages * kStageBytes;
+  const uint32_t store_base = smem_base + kStages * P::kStageBytes;
 
   Prof<kProfile> prof;
   if constexpr (kProfile) {
@@ -207,7 +213,9 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint32_t full_leader = cluster_map(smem_u32(&bar_full[0]), 0);
+      const uint32_t empty_peer = cluster_map(smem_u32(&bar_empty[0]), 1);
       uint32_t stage = 0, phase = 0;
+      uint32_t filled = 0;  // ring slots this producer has filled so far
       bool ok = true;
       for (int t = pair; ok && t < tiles; t += npairs) {
         int tm, tn;
@@ -220,12 +228,21 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
             ok = false;
             break;
           }
+          // The MMA commits a freed slot only to the leader's empty barrier
+          // (one tcgen05.commit per stage); the leader's producer passes each
+          // completion on to the peer's empty barrier.
+          if (rank == 0 && filled >= (uint32_t)kStages) mbar_arrive_cluster(empty_peer + stage * 8u);
+          ++filled;
           if constexpr (kProfile) { prof.stop(); prof.start(kTagIssueTMA); }
           const uint32_t fb = full_leader + stage * 8u;
-          const uint32_t sa = smem_base + stage * kStageBytes;
-          mbar_arrive_expect_tx_cluster(fb, kStageBytes);
-          tma_load_2d_pair(sa, &tmap_a, kb * kBlockK, a_row, fb);
-          tma_load_2d_pair(sa + kStageBytesA, &tmap_b, kb * kBlockK, b_row, fb);
+          const uint32_t sa = smem_base + stage * P::kStageBytes;
+          mbar_arrive_expect_tx_cluster(fb, P::kStageBytes);
+#pragma unroll
+          for (int sl = 0; sl < kSlabs; ++sl) {
+            const int x = kb * P::kBK + sl * kSlabK;
+            tma_load_2d_pair(sa + sl * kSlabBytes, &tmap_a, x, a_row, fb);
+            tma_load_2d_pair(sa + P::kBytesA + sl * kSlabBytes, &tmap_b, x, b_row, fb);
+          }
           if constexpr (kProfile) prof.stop();
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
@@ -238,7 +255,6 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     if (rank == 0 && lane == 0) {
       const uint32_t idesc = make_idesc_bf16_f32(kPairM, kPairN);
       const uint32_t empty_self = cluster_map(smem_u32(&bar_empty[0]), 0);
-      const uint32_t empty_peer = cluster_map(smem_u32(&bar_empty[0]), 1);
       const uint32_t accf_self = cluster_map(smem_u32(&bar_acc_full[0]), 0);
       const uint32_t accf_peer = cluster_map(smem_u32(&bar_acc_full[0]), 1);
       uint32_t stage = 0, phase = 0;
@@ -260,17 +276,19 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           }
           tc_fence_after_sync();
           if constexpr (kProfile) { prof.stop(); prof.start(kTagIssueMMA); }
-          const uint32_t sa = smem_base + stage * kStageBytes;
-          const uint64_t adesc = make_sdesc_k128(sa);
-          const uint64_t bdesc = make_sdesc_k128(sa + kStageBytesA);
+          const uint32_t sa = smem_base + stage * P::kStageBytes;
 #pragma unroll
-          for (int k = 0; k < kBlockK / kMmaK; ++k) {
-            // +32 B per K16 step inside the 128 B swizzled row (>>4 => +2)
-            umma_bf16_pair(d_tmem, adesc + 2ull * k, bdesc + 2ull * k, idesc,
-                           (kb | k) != 0 ? 1u : 0u);
+          for (int sl = 0; sl < kSlabs; ++sl) {
+            const uint64_t adesc = make_sdesc_k128(sa + sl * kSlabBytes);
+            const uint64_t bdesc = make_sdesc_k128(sa + P::kBytesA + sl * kSlabBytes);
+#pragma unroll
+            for (int k = 0; k < kSlabK / kMmaK; ++k) {
+              // +32 B per K16 step inside the 128 B swizzled row (>>4 => +2)
+              umma_bf16_pair(d_tmem, adesc + 2ull * k, bdesc + 2ull * k, idesc,
+                             (kb | sl | k) != 0 ? 1u : 0u);
+            }
           }
           umma_commit_pair(empty_self + stage * 8u);
-          umma_commit_pair(empty_peer + stage * 8u);
           if constexpr (kProfile) prof.stop();
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }

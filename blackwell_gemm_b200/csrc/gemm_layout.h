@@ -27,22 +27,34 @@ constexpr int kPairM = 256;        // rows of C per pair tile
 constexpr int kPairN = 256;        // columns of C per pair tile
 constexpr int kCtaM = 128;         // rows of A (and of C) owned by one CTA
 constexpr int kCtaN = 128;         // rows of B loaded by one CTA
-constexpr int kBlockK = 64;        // K elements per pipeline stage (= one 128 B swizzle row)
+constexpr int kSlabK = 64;         // K elements per 128 B swizzle slab (one TMA box)
+constexpr int kSlabBytes = 128 * kSlabK * 2;   // 16 KiB: one 128-row operand slab
 constexpr int kMmaK = 16;          // K per tcgen05.mma kind::f16
-constexpr int kStages = 6;         // shared-memory ring depth
 constexpr int kAccBufs = 2;        // TMEM accumulator buffers
 constexpr int kTmemCols = kAccBufs * kPairN;   // 512 = the whole TMEM of an SM
 constexpr int kStoreCols = 64;     // epilogue chunk width (one 128 B swizzle row of bf16)
 constexpr int kEpiWarps = 4;       // epilogue warps (one per TMEM lane quarter)
 constexpr int kWarps = 2 + kEpiWarps;          // producer, MMA, 4 x epilogue
 constexpr int kThreads = kWarps * 32;
-
-constexpr int kStageBytesA = kCtaM * kBlockK * 2;          // 16 KiB
-constexpr int kStageBytesB = kCtaN * kBlockK * 2;          // 16 KiB
-constexpr int kStageBytes = kStageBytesA + kStageBytesB;   // 32 KiB per CTA per stage
 constexpr int kStoreBufBytes = 32 * kStoreCols * 2;        // 4 KiB: 32 rows x 64 columns
 constexpr int kStoreBytes = kEpiWarps * 2 * kStoreBufBytes; // 2 buffers per epilogue warp
-constexpr int kSmemBytes = kStages * kStageBytes + kStoreBytes + 1024;  // +1024 for 1 KiB alignment
+constexpr int kSmemBudget = 227 * 1024;                    // opt-in shared memory per CTA
+constexpr int kSmemReserve = 1024 + 1024;                  // 1 KiB alignment + static/barriers
+
+// Pipeline shape for a K block of kSlabs x 64 elements per stage.  A stage
+// holds kSlabs slabs of A then kSlabs slabs of B (16 KiB each, 1 KiB
+// aligned); the ring depth is whatever fits beside the epilogue staging.
+// Fewer, deeper stages mean fewer barrier round trips and tcgen05.commits per
+// MMA; more stages mean finer-grained slot recycling.
+template <int kSlabs>
+struct Pipe {
+  static constexpr int kBK = kSlabs * kSlabK;
+  static constexpr int kBytesA = kSlabs * kSlabBytes;
+  static constexpr int kStageBytes = 2 * kBytesA;
+  static constexpr int kStages = (kSmemBudget - kStoreBytes - kSmemReserve) / kStageBytes;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kStoreBytes + 1024;
+  static_assert(kStages >= 2, "pipeline needs at least two stages");
+};
 
 // ---------------------------------------------------------------------------
 // tcgen05 instruction descriptor for kind::f16 (PTX ISA "Instruction

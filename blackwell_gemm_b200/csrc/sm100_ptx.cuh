@@ -73,24 +73,34 @@ __device__ __forceinline__ void fence_mbar_init_cluster() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// Suspend-time hint of a barrier poll: a thread whose barrier phase has not
+// completed sleeps until it does or until this many nanoseconds pass, instead
+// of re-polling.  Polling warps would otherwise take issue slots from the
+// single thread that feeds the tensor core on the same scheduler.
+constexpr uint32_t kPollSuspendNs = 1000000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+      : "=r"(done) : "r"(bar), "r"(parity), "n"(kPollSuspendNs) : "memory");
   return done != 0;
 }
 
 // Arrive on a barrier given by its shared::cluster address (local or peer).
+// Release semantics at CTA scope: the data these arrivals publish is either
+// written by the async proxy (TMA, tracked by the transaction count) or is
+// TMEM ordered by tcgen05 fences, so no cluster-scope memory fence is needed
+// -- and one per pipeline stage would stall the issuing thread.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];"
+  asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];"
                :: "r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;"
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cluster.b64 _, [%0], %1;"
                :: "r"(bar), "r"(bytes) : "memory");
 }
 

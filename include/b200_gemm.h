@@ -66,6 +66,14 @@ int b200_gemm_profile_rows(int M, int N, int K, int* rows);
  * counterpart (the reference's waits never give up, kernel_v8.cu:60-76). */
 int b200_gemm_device_status(int clear, int* status_out);
 
+/* Process-wide tuning: K slabs of 64 per pipeline stage (1: 6 stages of
+ * K=64, 2: 3 stages of K=128) and the band height, in 256-row tiles, of the
+ * persistent raster.  0 keeps a value.  Defaults come from B200_GEMM_SLABS /
+ * B200_GEMM_GROUP.  Plays the role of the reference's GEMM_L2_A/GEMM_L2_B
+ * environment knobs (src/kernels/kernel_v8.cu:11-31). */
+int b200_gemm_set_tuning(int stage_slabs, int raster_group);
+int b200_gemm_get_tuning(int* stage_slabs, int* raster_group);
+
 /* Upper bound, in nanoseconds, on any single pipeline wait inside the GEMM
  * kernels of this process (default 2 s).  No reference counterpart. */
 int b200_gemm_set_wait_timeout_ns(unsigned long long timeout_ns);

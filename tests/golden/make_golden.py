@@ -3,7 +3,7 @@ reference's own v8 kernel (matmul_v8, src/kernels/kernel_v8.cu:830-833,
 compiled from its sources into oracle/_ref/libref_gemm.so by oracle/build.py)
 on the seeded inputs of tests/golden/cases.py.
 
-Run once on a B200:  python tests/golden/make_golden.py
+Run once on a B200:  python tests/golden/make_golden.py [--out DIR]
 Also records the v6 kernel's output and checks v6 == v8 on the exact cases,
 as a sanity check of the reference build itself.
 """
@@ -36,17 +36,19 @@ def run_ref(version, A, Bt):
 
 
 def main():
+    out_dir = Path(sys.argv[sys.argv.index("--out") + 1]) if "--out" in sys.argv else cases.HERE
+    out_dir.mkdir(parents=True, exist_ok=True)
     for case in cases.CASES:
         A, Bt = cases.inputs(case)
         C8 = run_ref("v8", A, Bt)
         C6 = run_ref("v6", A, Bt)
         if case["kind"] == "exact":
             assert np.array_equal(C8, C6), f"{case['name']}: reference v6 != v8 on exact inputs"
-        np.savez_compressed(cases.path(case), C=C8, kind=case["kind"], version="v8",
+        np.savez_compressed(out_dir / cases.path(case).name, C=C8, kind=case["kind"], version="v8",
                             input_sha256=cases.input_digest(A, Bt),
                             M=case["M"], N=case["N"], K=case["K"], seed=case["seed"],
                             std=case["std"])
-        print(f"{case['name']}: wrote {cases.path(case).name} "
+        print(f"{case['name']}: wrote {out_dir / cases.path(case).name} "
               f"(v6==v8 on {np.mean(C6 == C8) * 100:.2f}% of elements)")
 
 
