@@ -72,7 +72,8 @@ std::atomic<int> g_slabs{-1};
 int raster_group() {
   int g = g_group.load();
   if (g < 0) {
-    g = env_int("B200_GEMM_GROUP", 8, 1, 1 << 16);
+    g = env_int("B200_GEMM_GROUP", 8, -(1 << 16), 1 << 16);
+    if (g == 0) g = 8;
     g_group.store(g);
   }
   return g;
@@ -302,9 +303,9 @@ int b200_gemm_device_status(int clear, int* status_out) {
 }
 
 int b200_gemm_set_tuning(int stage_slabs, int raster_group) {
-  if (stage_slabs < 0 || stage_slabs > 2 || raster_group < 0) return B200_ERR_INVALID_ARGUMENT;
+  if (stage_slabs < 0 || stage_slabs > 2) return B200_ERR_INVALID_ARGUMENT;
   if (stage_slabs > 0) g_slabs.store(stage_slabs);
-  if (raster_group > 0) g_group.store(raster_group);
+  if (raster_group != 0) g_group.store(raster_group);
   return B200_OK;
 }
 

@@ -85,21 +85,31 @@ B200_HD uint64_t make_sdesc_k128(uint32_t smem_addr) {
 // ---------------------------------------------------------------------------
 // Persistent tile rasteriser.  Pair tiles are numbered 0..tiles-1 and pair p
 // of P processes tiles p, p+P, p+2P, ...; consecutive numbers are therefore
-// in flight at the same time.  Numbers walk down a band of `group` tile-rows
-// before moving one tile-column right, so the ~74 tiles in flight touch about
-// group + 74/group distinct 256-row blocks of A and B instead of 2*74: that
-// is what keeps the working set of one wave inside the 126 MB L2.  The
-// reference instead deals a Hilbert curve over the tile grid
+// in flight at the same time.  Numbers walk across a band of |group| tiles
+// of one dimension before stepping along the other, so the ~74 tiles in
+// flight touch about |group| + 74/|group| distinct 256-row blocks of A and B
+// instead of 2*74: that keeps the working set of one wave inside the 126 MB
+// L2.  group > 0 makes bands of tile-rows (sweeping N), group < 0 bands of
+// tile-columns (sweeping M).  Odd bands sweep backwards (serpentine), so the
+// last operand blocks of one band are the first of the next.  The reference
+// instead deals a Hilbert curve over the tile grid
 // (kernel_v8.cu:338-358,796-820); both are permutations of the grid.
 B200_HD void tile_coord(int t, int tiles_m, int tiles_n, int group, int* tm, int* tn) {
-  const int band_tiles = group * tiles_n;
+  const bool cols = group < 0;
+  const int g = cols ? -group : group;
+  const int banded = cols ? tiles_n : tiles_m;   // dimension cut into bands
+  const int swept = cols ? tiles_m : tiles_n;    // dimension each band sweeps
+  const int band_tiles = g * swept;
   const int band = t / band_tiles;
-  const int first_m = band * group;
-  int rows = tiles_m - first_m;
-  if (rows > group) rows = group;
+  const int first = band * g;
+  int width = banded - first;
+  if (width > g) width = g;
   const int r = t - band * band_tiles;
-  *tm = first_m + r % rows;
-  *tn = r / rows;
+  const int a = first + r % width;
+  int b = r / width;
+  if (band & 1) b = swept - 1 - b;
+  *tm = cols ? b : a;
+  *tn = cols ? a : b;
 }
 
 }  // namespace b200

@@ -67,8 +67,9 @@ int b200_gemm_profile_rows(int M, int N, int K, int* rows);
 int b200_gemm_device_status(int clear, int* status_out);
 
 /* Process-wide tuning: K slabs of 64 per pipeline stage (1: 6 stages of
- * K=64, 2: 3 stages of K=128) and the band height, in 256-row tiles, of the
- * persistent raster.  0 keeps a value.  Defaults come from B200_GEMM_SLABS /
+ * K=64, 2: 3 stages of K=128) and the band width, in 256-wide tiles, of the
+ * persistent raster (positive: bands of tile-rows, negative: bands of
+ * tile-columns).  0 keeps a value.  Defaults come from B200_GEMM_SLABS /
  * B200_GEMM_GROUP.  Plays the role of the reference's GEMM_L2_A/GEMM_L2_B
  * environment knobs (src/kernels/kernel_v8.cu:11-31). */
 int b200_gemm_set_tuning(int stage_slabs, int raster_group);

@@ -55,7 +55,8 @@ def test_smem_descriptor_k_advance_is_plus_two():
 
 
 @pytest.mark.parametrize("tm,tn,group", [(32, 32, 8), (1, 1, 8), (4, 64, 8), (33, 7, 8),
-                                          (5, 5, 16), (112, 24, 8), (32, 32, 1), (3, 9, 2)])
+                                          (5, 5, 16), (112, 24, 8), (32, 32, 1), (3, 9, 2),
+                                          (32, 32, -8), (7, 33, -8), (24, 112, -4), (9, 3, -2)])
 def test_raster_is_a_permutation(tm, tn, group):
     seen = set()
     for t in range(tm * tn):
@@ -76,6 +77,17 @@ def test_raster_bands_keep_wave_working_set_small():
             ms.add(m)
             ns.add(n)
         assert len(ms) + len(ns) <= 8 + 8 + 11
+
+
+def test_raster_serpentine_band_transition_reuses_blocks():
+    # the last tile of band 0 and the first of band 1 share a column block
+    tm, tn, g = 32, 32, 8
+    last = capi.tile_coord(g * tn - 1, tm, tn, g)
+    first = capi.tile_coord(g * tn, tm, tn, g)
+    assert last[1] == first[1]
+    last = capi.tile_coord(g * tm - 1, tm, tn, -g)
+    first = capi.tile_coord(g * tm, tm, tn, -g)
+    assert last[0] == first[0]
 
 
 def test_persistent_assignment_covers_all_tiles_once():
