@@ -41,8 +41,8 @@ SIGNATURES = {
     "b200_gemm_profile_rows": (_i, [_i, _i, _i, _ip]),
     "b200_gemm_device_status": (_i, [_i, _ip]),
     "b200_gemm_set_wait_timeout_ns": (_i, [_ull]),
-    "b200_gemm_set_tuning": (_i, [_i, _i]),
-    "b200_gemm_get_tuning": (_i, [_ip, _ip]),
+    "b200_gemm_set_tuning": (_i, [_i, _i, _i]),
+    "b200_gemm_get_tuning": (_i, [_ip, _ip, _ip]),
     "b200_gemm_wait_probe": (_i, [_ull, _vp]),
     "b200_gemm_status_string": (ctypes.c_char_p, [_i]),
     "b200_gemm_tile_coord": (None, [_i, _i, _i, _i, _ip, _ip]),
@@ -111,14 +111,18 @@ def set_wait_timeout_ns(ns: int) -> None:
     check(lib().b200_gemm_set_wait_timeout_ns(int(ns)), "set_wait_timeout_ns")
 
 
-def set_tuning(stage_slabs: int = 0, raster_group: int = 0) -> None:
-    check(lib().b200_gemm_set_tuning(int(stage_slabs), int(raster_group)), "set_tuning")
+def set_tuning(tile_n: int = 0, stage_slabs: int = 0, raster_group: int = 0) -> None:
+    """tile_n: 256, 512, -1 (per shape) or 0 (keep); stage_slabs: 1, 2 or 0;
+    raster_group: band width in tiles (negative: column bands) or 0."""
+    check(lib().b200_gemm_set_tuning(int(tile_n), int(stage_slabs), int(raster_group)),
+          "set_tuning")
 
 
 def get_tuning() -> dict:
-    s, g = ctypes.c_int(0), ctypes.c_int(0)
-    check(lib().b200_gemm_get_tuning(ctypes.byref(s), ctypes.byref(g)), "get_tuning")
-    return {"stage_slabs": s.value, "raster_group": g.value}
+    t, s, g = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    check(lib().b200_gemm_get_tuning(ctypes.byref(t), ctypes.byref(s), ctypes.byref(g)),
+          "get_tuning")
+    return {"tile_n": t.value, "stage_slabs": s.value, "raster_group": g.value}
 
 
 def wait_probe(timeout_ns: int, stream: int = 0) -> int:

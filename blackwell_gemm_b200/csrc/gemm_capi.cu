@@ -1,15 +1,17 @@
 // C-ABI launcher for the sm_100a BF16 GEMM (declarations: include/b200_gemm.h).
 //
-// Per call: validate the operands, encode three TMA tensor maps (A, B: 2-D,
-// box 64 x 128, 128 B swizzle, zero fill out of bounds; C: 2-D, box
+// Per call: validate the operands, pick a kernel configuration (pair tile
+// 256 x 256 or 256 x 512, stage depth), encode three TMA tensor maps (A, B:
+// 2-D, box 64 x 128, 128 B swizzle, zero fill out of bounds; C: 2-D, box
 // 64 x 32, 128 B swizzle), then launch the persistent kernel on the caller's
 // stream.  The reference does the same three steps per call with 3-D maps and
 // without validation (kernel_v8.cu:775-828).
 //
-// Per device, once: check the architecture, raise the kernel's shared-memory
-// limit, ask the occupancy API how many 2-CTA clusters can be resident at
-// once (the persistent grid size) and allocate the 4-byte device error word.
-// The reference keeps a device-blind static cache instead (kernel_v8.cu:796-820).
+// Per device, once: check the architecture, raise each configuration's
+// shared-memory limit, ask the occupancy API how many 2-CTA clusters can be
+// resident at once (the persistent grid size) and allocate the 4-byte device
+// error word.  The reference keeps a device-blind static cache instead
+// (kernel_v8.cu:796-820).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -42,14 +44,24 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
+// Kernel configurations: {K slabs per stage, N sub-tiles per pair tile}.
+enum Variant { kV256x64 = 0, kV256x128 = 1, kV512x64 = 2, kNumVariants = 3 };
+constexpr int kVariantSlabs[kNumVariants] = {1, 2, 1};
+constexpr int kVariantNSub[kNumVariants] = {1, 1, 2};
+
+template <int V>
+struct VariantCfg {
+  using C = Cfg<kVariantSlabs[V], kVariantNSub[V]>;
+};
+
 constexpr int kMaxDevices = 64;
 
 struct DeviceState {
   bool ready = false;
   int init_status = B200_OK;
   int sms = 0;
-  int max_pairs = 0;     // co-resident 2-CTA clusters of the GEMM kernel
-  int* status = nullptr; // device error word
+  int max_pairs[kNumVariants] = {0, 0, 0};  // co-resident 2-CTA clusters per variant
+  int* status = nullptr;                    // device error word
 };
 
 std::mutex g_mu;
@@ -63,20 +75,22 @@ int env_int(const char* name, int fallback, int lo, int hi) {
   return (x < lo || x > hi) ? fallback : x;
 }
 
-// Tuning knobs, process-wide: band height (tile-rows) of the grouped raster
-// and K slabs (64 elements each) per pipeline stage.  Initialised from
-// B200_GEMM_GROUP / B200_GEMM_SLABS, changeable through b200_gemm_set_tuning.
-std::atomic<int> g_group{-1};
+// Tuning knobs, process-wide: pair-tile width (0 = chosen per shape, 256,
+// 512), K slabs per stage for 256-wide tiles (1 or 2) and the raster band
+// width.  Initialised from B200_GEMM_TILE_N / B200_GEMM_SLABS /
+// B200_GEMM_GROUP, changeable through b200_gemm_set_tuning.
+std::atomic<int> g_tile_n{-1};
 std::atomic<int> g_slabs{-1};
+std::atomic<int> g_group{0};
 
-int raster_group() {
-  int g = g_group.load();
-  if (g < 0) {
-    g = env_int("B200_GEMM_GROUP", 8, -(1 << 16), 1 << 16);
-    if (g == 0) g = 8;
-    g_group.store(g);
+int tuning_tile_n() {
+  int v = g_tile_n.load();
+  if (v < 0) {
+    v = env_int("B200_GEMM_TILE_N", 0, 0, 512);
+    if (v != 256 && v != 512) v = 0;
+    g_tile_n.store(v);
   }
-  return g;
+  return v;
 }
 
 int stage_slabs() {
@@ -88,12 +102,22 @@ int stage_slabs() {
   return s;
 }
 
-template <typename K>
-int max_active_pairs(K kernel, int sms, int smem_bytes, int* out) {
+int raster_group() {
+  int g = g_group.load();
+  if (g == 0) {
+    g = env_int("B200_GEMM_GROUP", -8, -(1 << 16), 1 << 16);
+    if (g == 0) g = -8;
+    g_group.store(g);
+  }
+  return g;
+}
+
+template <int V>
+int query_pairs(int sms, int* out) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * sms, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.blockDim = dim3(VariantCfg<V>::C::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = VariantCfg<V>::C::kSmemBytes;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
@@ -102,16 +126,44 @@ int max_active_pairs(K kernel, int sms, int smem_bytes, int* out) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) return B200_ERR_LAUNCH;
+  if (cudaOccupancyMaxActiveClusters(
+          &n, gemm_bf16_pair_kernel<false, kVariantSlabs[V], kVariantNSub[V]>, &cfg) !=
+      cudaSuccess)
+    return B200_ERR_LAUNCH;
   *out = n;
   return B200_OK;
 }
 
-template <bool kProfile, int kSlabs>
-cudaError_t set_smem_limit() {
-  return cudaFuncSetAttribute(gemm_bf16_pair_kernel<kProfile, kSlabs>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              Pipe<kSlabs>::kSmemBytes);
+template <int V>
+bool set_smem_limits() {
+  constexpr int S = kVariantSlabs[V], NS = kVariantNSub[V];
+  constexpr int bytes = VariantCfg<V>::C::kSmemBytes;
+  return cudaFuncSetAttribute(gemm_bf16_pair_kernel<false, S, NS>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
+             cudaSuccess &&
+         cudaFuncSetAttribute(gemm_bf16_pair_kernel<true, S, NS>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
+}
+
+int init_device(DeviceState& d, int dev) {
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return B200_ERR_UNSUPPORTED_DEVICE;
+  if (prop.major != 10 || prop.minor != 0) return B200_ERR_UNSUPPORTED_DEVICE;  // sm_100a only
+  if (encode_tiled() == nullptr) return B200_ERR_TENSOR_MAP;
+  d.sms = prop.multiProcessorCount;
+  if (!set_smem_limits<kV256x64>() || !set_smem_limits<kV256x128>() ||
+      !set_smem_limits<kV512x64>())
+    return B200_ERR_LAUNCH;
+  if (query_pairs<kV256x64>(d.sms, &d.max_pairs[kV256x64]) != B200_OK ||
+      query_pairs<kV256x128>(d.sms, &d.max_pairs[kV256x128]) != B200_OK ||
+      query_pairs<kV512x64>(d.sms, &d.max_pairs[kV512x64]) != B200_OK)
+    return B200_ERR_LAUNCH;
+  for (int v = 0; v < kNumVariants; ++v)
+    if (d.max_pairs[v] < 1) return B200_ERR_LAUNCH;
+  if (cudaMalloc(&d.status, sizeof(int)) != cudaSuccess ||
+      cudaMemset(d.status, 0, sizeof(int)) != cudaSuccess)
+    return B200_ERR_LAUNCH;
+  return B200_OK;
 }
 
 int device_state(DeviceState** out) {
@@ -125,36 +177,37 @@ int device_state(DeviceState** out) {
   DeviceState& d = g_dev[dev];
   if (!d.ready) {
     d.ready = true;
-    cudaDeviceProp prop;
-    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
-      d.init_status = B200_ERR_UNSUPPORTED_DEVICE;
-    } else if (prop.major != 10 || prop.minor != 0) {
-      d.init_status = B200_ERR_UNSUPPORTED_DEVICE;  // built for sm_100a only
-    } else if (encode_tiled() == nullptr) {
-      d.init_status = B200_ERR_TENSOR_MAP;
-    } else {
-      d.sms = prop.multiProcessorCount;
-      int st = B200_OK;
-      if (set_smem_limit<false, 1>() != cudaSuccess || set_smem_limit<true, 1>() != cudaSuccess ||
-          set_smem_limit<false, 2>() != cudaSuccess || set_smem_limit<true, 2>() != cudaSuccess)
-        st = B200_ERR_LAUNCH;
-      // Every variant runs one CTA per SM, so one occupancy query sizes all.
-      if (st == B200_OK)
-        st = max_active_pairs(gemm_bf16_pair_kernel<false, 1>, d.sms, Pipe<1>::kSmemBytes,
-                              &d.max_pairs);
-      if (st == B200_OK && d.max_pairs < 1) st = B200_ERR_LAUNCH;
-      if (st == B200_OK) {
-        if (cudaMalloc(&d.status, sizeof(int)) != cudaSuccess ||
-            cudaMemset(d.status, 0, sizeof(int)) != cudaSuccess)
-          st = B200_ERR_LAUNCH;
-      }
-      d.init_status = st;
-    }
+    d.init_status = init_device(d, dev);
     if (d.init_status != B200_OK) cudaGetLastError();
   }
   if (d.init_status != B200_OK) return d.init_status;
   *out = &d;
   return B200_OK;
+}
+
+long long ceil_div(long long a, long long b) { return (a + b - 1) / b; }
+
+// Fraction of pair-slots doing useful work over the persistent waves.
+double wave_efficiency(long long tiles, int pairs) {
+  const long long waves = ceil_div(tiles, pairs);
+  return waves > 0 ? (double)tiles / (double)(waves * pairs) : 0.0;
+}
+
+// Configuration for an M x N problem.  512-wide pair tiles read 25% fewer
+// operand bytes per FLOP through L2 (one A slab feeds two MMAs), which under
+// the 1 kW power cap turns into clock; they are chosen unless halving the
+// tile count costs wave efficiency or leaves pairs idle.
+int choose_variant(int M, int N, const int* max_pairs) {
+  const int tn = tuning_tile_n();
+  if (tn == 512) return kV512x64;
+  const int v256 = stage_slabs() == 2 ? kV256x128 : kV256x64;
+  if (tn == 256) return v256;
+  const long long t256 = ceil_div(M, kPairM) * ceil_div(N, kSubN);
+  const long long t512 = ceil_div(M, kPairM) * ceil_div(N, 2 * kSubN);
+  const int p256 = max_pairs ? max_pairs[v256] : 74;
+  const int p512 = max_pairs ? max_pairs[kV512x64] : 74;
+  if (t512 < p512) return v256;
+  return wave_efficiency(t512, p512) + 0.02 >= wave_efficiency(t256, p256) ? kV512x64 : v256;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -182,8 +235,8 @@ int encode_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = encode_tiled()(
       map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-      l2_promotion(), CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, l2_promotion(),
+      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TENSOR_MAP;
 }
 
@@ -197,6 +250,19 @@ int validate(const void* A, const void* B, void* C, int M, int N, int K, int lda
   if (K > 0 && (!aligned16(A) || !aligned16(B) || (lda & 7) || (ldb & 7)))
     return B200_ERR_ALIGNMENT;
   return B200_OK;
+}
+
+template <bool kProfile, int V>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmArgs args,
+           const DeviceState& d, cudaStream_t stream) {
+  using C = typename VariantCfg<V>::C;
+  args.tiles_n = (int)ceil_div(args.N, C::kTileN);
+  args.k_blocks = (int)ceil_div(args.K, C::kBK);
+  const long long tiles = (long long)args.tiles_m * args.tiles_n;
+  const int pairs = (int)(tiles < d.max_pairs[V] ? tiles : d.max_pairs[V]);
+  gemm_bf16_pair_kernel<kProfile, kVariantSlabs[V], kVariantNSub[V]>
+      <<<2 * pairs, C::kThreads, C::kSmemBytes, stream>>>(ta, tb, tc, args);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
 }
 
 template <bool kProfile>
@@ -221,29 +287,31 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda
       encode_2d(&tc, C, N, M, ldc, kStoreCols, 32) != B200_OK)
     return B200_ERR_TENSOR_MAP;
 
-  const int slabs = stage_slabs();
-  const int bk = slabs * kSlabK;
   GemmArgs args;
   args.M = M;
   args.N = N;
   args.K = K;
-  args.tiles_m = (M + kPairM - 1) / kPairM;
-  args.tiles_n = (N + kPairN - 1) / kPairN;
-  args.k_blocks = (K + bk - 1) / bk;
+  args.tiles_m = (int)ceil_div(M, kPairM);
+  args.tiles_n = 0;
+  args.k_blocks = 0;
   args.group = raster_group();
   args.status = d->status;
   args.timeout_ns = g_timeout_ns.load();
   args.prof = prof;
   args.prof_entries = prof_entries;
-  const long long tiles = (long long)args.tiles_m * args.tiles_n;
-  const int pairs = (int)(tiles < d->max_pairs ? tiles : d->max_pairs);
-  if (slabs == 2)
-    gemm_bf16_pair_kernel<kProfile, 2><<<2 * pairs, kThreads, Pipe<2>::kSmemBytes, stream>>>(
-        ta, tb, tc, args);
-  else
-    gemm_bf16_pair_kernel<kProfile, 1><<<2 * pairs, kThreads, Pipe<1>::kSmemBytes, stream>>>(
-        ta, tb, tc, args);
-  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
+  switch (choose_variant(M, N, d->max_pairs)) {
+    case kV256x128: return launch<kProfile, kV256x128>(ta, tb, tc, args, *d, stream);
+    case kV512x64: return launch<kProfile, kV512x64>(ta, tb, tc, args, *d, stream);
+    default: return launch<kProfile, kV256x64>(ta, tb, tc, args, *d, stream);
+  }
+}
+
+template <int V>
+void shape_of(long long* tile_n, int* smem, int* threads) {
+  using C = typename VariantCfg<V>::C;
+  *tile_n = C::kTileN;
+  *smem = C::kSmemBytes;
+  *threads = C::kThreads;
 }
 
 }  // namespace
@@ -265,25 +333,31 @@ int b200_gemm_bf16_profile(const void* A, const void* B, void* C, int M, int N, 
 int b200_gemm_launch_shape(int M, int N, int K, int* tiles, int* grid, int* smem_bytes,
                            int* threads) {
   if (M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARGUMENT;
-  const long long t = (long long)((M + kPairM - 1) / kPairM) * ((N + kPairN - 1) / kPairN);
+  DeviceState* d = nullptr;
+  const bool have_dev = device_state(&d) == B200_OK;
+  const int v = choose_variant(M, N, have_dev ? d->max_pairs : nullptr);
+  long long tile_n;
+  int smem, thr;
+  if (v == kV512x64) shape_of<kV512x64>(&tile_n, &smem, &thr);
+  else if (v == kV256x128) shape_of<kV256x128>(&tile_n, &smem, &thr);
+  else shape_of<kV256x64>(&tile_n, &smem, &thr);
+  const long long t = ceil_div(M, kPairM) * ceil_div(N, tile_n);
   if (tiles) *tiles = (int)t;
-  if (smem_bytes) *smem_bytes = stage_slabs() == 2 ? Pipe<2>::kSmemBytes : Pipe<1>::kSmemBytes;
-  if (threads) *threads = kThreads;
+  if (smem_bytes) *smem_bytes = smem;
+  if (threads) *threads = thr;
   if (grid) {
     *grid = 0;
-    DeviceState* d = nullptr;
-    if (t > 0 && K > 0 && device_state(&d) == B200_OK)
-      *grid = 2 * (int)(t < d->max_pairs ? t : d->max_pairs);
+    if (t > 0 && K > 0 && have_dev) *grid = 2 * (int)(t < d->max_pairs[v] ? t : d->max_pairs[v]);
   }
   return B200_OK;
 }
 
 int b200_gemm_profile_rows(int M, int N, int K, int* rows) {
   if (!rows) return B200_ERR_INVALID_ARGUMENT;
-  int grid = 0;
-  const int st = b200_gemm_launch_shape(M, N, K, nullptr, &grid, nullptr, nullptr);
+  int grid = 0, threads = 0;
+  const int st = b200_gemm_launch_shape(M, N, K, nullptr, &grid, nullptr, &threads);
   if (st != B200_OK) return st;
-  *rows = grid * kWarps;
+  *rows = grid * (threads / 32);
   return B200_OK;
 }
 
@@ -302,14 +376,19 @@ int b200_gemm_device_status(int clear, int* status_out) {
   return B200_OK;
 }
 
-int b200_gemm_set_tuning(int stage_slabs, int raster_group) {
-  if (stage_slabs < 0 || stage_slabs > 2) return B200_ERR_INVALID_ARGUMENT;
+int b200_gemm_set_tuning(int tile_n, int stage_slabs, int raster_group) {
+  if ((tile_n != 0 && tile_n != -1 && tile_n != 256 && tile_n != 512) || stage_slabs < 0 ||
+      stage_slabs > 2)
+    return B200_ERR_INVALID_ARGUMENT;
+  if (tile_n == -1) g_tile_n.store(0);
+  else if (tile_n != 0) g_tile_n.store(tile_n);
   if (stage_slabs > 0) g_slabs.store(stage_slabs);
   if (raster_group != 0) g_group.store(raster_group);
   return B200_OK;
 }
 
-int b200_gemm_get_tuning(int* stage_slabs_out, int* raster_group_out) {
+int b200_gemm_get_tuning(int* tile_n, int* stage_slabs_out, int* raster_group_out) {
+  if (tile_n) *tile_n = tuning_tile_n();
   if (stage_slabs_out) *stage_slabs_out = stage_slabs();
   if (raster_group_out) *raster_group_out = raster_group();
   return B200_OK;

@@ -4,19 +4,23 @@
 //      N x K buffer", matmul.cpp:25-39)
 //   C  M x N bf16, row stride ldc, fp32 accumulation, round-to-nearest-even
 //
-// One 2-CTA cluster ("pair") owns a 256x256 tile of C at a time.  Warp roles
-// per CTA (192 threads):
-//   warp 0     TMA producer: fills a 6-stage ring of {A 128x64, B 128x64}
+// One 2-CTA cluster ("pair") owns a 256 x (256 * kNSub) tile of C at a time
+// (configurations in gemm_layout.h, Cfg).  Warp roles per CTA:
+//   warp 0     TMA producer: fills the shared-memory ring of {A 128 x BK,
+//              kNSub x B 128 x BK}
 //   warp 1     TMEM owner; in the pair leader also the MMA issuer
-//              (tcgen05.mma.cta_group::2, 4 x K16 per stage)
-//   warps 2-5  epilogue: tcgen05.ld -> bf16 -> swizzled smem -> TMA store,
-//              one warp per TMEM lane quarter, each with its own two
-//              4 KiB staging buffers so no epilogue warp waits for another
+//              (tcgen05.mma.cta_group::2, kNSub MMAs per K16 step)
+//   warps 2..  epilogue, 4 per N sub-tile: tcgen05.ld -> bf16 -> swizzled
+//              smem -> TMA store, one warp per (TMEM lane quarter, sub-tile),
+//              each with its own two 4 KiB staging buffers so no epilogue
+//              warp waits for another
 // Pipelines:
 //   full[s]/empty[s]        ring stage s (full lives in the leader: both
 //                           producers arrive on it; empty lives in each CTA)
-//   acc_full[b]/acc_empty[b] TMEM accumulator buffer b (2 buffers), so the
-//                           epilogue of tile i overlaps the MMAs of tile i+1
+//   acc_full[b]/acc_empty[b] TMEM accumulator b (two 256-column buffers for
+//                           256-wide tiles, so the epilogue of tile i
+//                           overlaps the MMAs of tile i+1; one 512-column
+//                           buffer for 512-wide tiles)
 // Reference behaviour followed: kernel_v8.cu:360-773 (same math, same tile,
 // same TMA/UMMA/epilogue data path); the scheduling here is a static
 // persistent walk over a grouped raster (gemm_layout.h) instead of cluster
@@ -138,14 +142,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <bool kProfile, int kSlabs>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+template <bool kProfile, int kSlabs, int kNSub>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<kSlabs, kNSub>::kThreads, 1)
 gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_c,
                       const GemmArgs args) {
-  using P = Pipe<kSlabs>;
+  using P = Cfg<kSlabs, kNSub>;
   constexpr int kStages = P::kStages;
+  constexpr int kAccBufs = P::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
   __shared__ alignas(8) uint64_t bar_full[kStages];
   __shared__ alignas(8) uint64_t bar_empty[kStages];
@@ -169,7 +174,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
   Prof<kProfile> prof;
   if constexpr (kProfile) {
     if (lane == 0) {
-      prof.init(args.prof, args.prof_entries, blockIdx.x * kWarps + warp);
+      prof.init(args.prof, args.prof_entries, blockIdx.x * P::kWarps + warp);
       prof.start(kTagSetup);
     }
   }
@@ -177,11 +182,11 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&bar_full[s]), 2);   // one expect_tx arrive per CTA
-      mbar_init(smem_u32(&bar_empty[s]), 1);  // one tcgen05.commit
+      mbar_init(smem_u32(&bar_empty[s]), 1);  // one tcgen05.commit (or its forward)
     }
     for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(smem_u32(&bar_acc_full[b]), 1);
-      mbar_init(smem_u32(&bar_acc_empty[b]), 2 * kEpiWarps);  // every epilogue warp of the pair
+      mbar_init(smem_u32(&bar_acc_empty[b]), 2 * P::kEpiWarps);  // every epilogue warp of the pair
     }
     mbar_init(smem_u32(&bar_drain), 1);
     abort_word = 0;
@@ -221,7 +226,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
         int tm, tn;
         tile_coord(t, args.tiles_m, args.tiles_n, args.group, &tm, &tn);
         const int a_row = tm * kPairM + (int)rank * kCtaM;
-        const int b_row = tn * kPairN + (int)rank * kCtaN;
+        const int b_row = tn * P::kTileN + (int)rank * kCtaN;
         for (int kb = 0; kb < args.k_blocks; ++kb) {
           if constexpr (kProfile) prof.start(kTagWaitMMA);
           if (!wait_bounded(smem_u32(&bar_empty[stage]), phase ^ 1u, wctx, kErrWaitEmpty)) {
@@ -241,7 +246,10 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           for (int sl = 0; sl < kSlabs; ++sl) {
             const int x = kb * P::kBK + sl * kSlabK;
             tma_load_2d_pair(sa + sl * kSlabBytes, &tmap_a, x, a_row, fb);
-            tma_load_2d_pair(sa + P::kBytesA + sl * kSlabBytes, &tmap_b, x, b_row, fb);
+#pragma unroll
+            for (int sub = 0; sub < kNSub; ++sub)
+              tma_load_2d_pair(sa + P::kBytesA + (sub * kSlabs + sl) * kSlabBytes, &tmap_b, x,
+                               b_row + sub * kSubN, fb);
           }
           if constexpr (kProfile) prof.stop();
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
@@ -253,7 +261,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     if (rank == 0 && lane == 0) {
-      const uint32_t idesc = make_idesc_bf16_f32(kPairM, kPairN);
+      const uint32_t idesc = make_idesc_bf16_f32(kPairM, kSubN);
       const uint32_t empty_self = cluster_map(smem_u32(&bar_empty[0]), 0);
       const uint32_t accf_self = cluster_map(smem_u32(&bar_acc_full[0]), 0);
       const uint32_t accf_peer = cluster_map(smem_u32(&bar_acc_full[0]), 1);
@@ -261,13 +269,13 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       int it = 0;
       bool ok = true;
       for (int t = pair; ok && t < tiles; t += npairs, ++it) {
-        const uint32_t buf = it & 1, acc_phase = (it >> 1) & 1;
+        const uint32_t buf = it % kAccBufs, acc_phase = (it / kAccBufs) & 1;
         if constexpr (kProfile) prof.start(kTagWaitEpilogue);
         if (!wait_bounded(smem_u32(&bar_acc_empty[buf]), acc_phase ^ 1u, wctx, kErrWaitAccEmpty))
           break;
         if constexpr (kProfile) prof.stop();
         tc_fence_after_sync();
-        const uint32_t d_tmem = tmem_base + buf * kPairN;
+        const uint32_t d_tmem = tmem_base + buf * P::kTileN;
         for (int kb = 0; kb < args.k_blocks; ++kb) {
           if constexpr (kProfile) prof.start(kTagWaitTMA);
           if (!wait_bounded(smem_u32(&bar_full[stage]), phase, wctx, kErrWaitFull)) {
@@ -280,12 +288,16 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
 #pragma unroll
           for (int sl = 0; sl < kSlabs; ++sl) {
             const uint64_t adesc = make_sdesc_k128(sa + sl * kSlabBytes);
-            const uint64_t bdesc = make_sdesc_k128(sa + P::kBytesA + sl * kSlabBytes);
 #pragma unroll
             for (int k = 0; k < kSlabK / kMmaK; ++k) {
-              // +32 B per K16 step inside the 128 B swizzled row (>>4 => +2)
-              umma_bf16_pair(d_tmem, adesc + 2ull * k, bdesc + 2ull * k, idesc,
-                             (kb | sl | k) != 0 ? 1u : 0u);
+#pragma unroll
+              for (int sub = 0; sub < kNSub; ++sub) {
+                const uint64_t bdesc =
+                    make_sdesc_k128(sa + P::kBytesA + (sub * kSlabs + sl) * kSlabBytes);
+                // +32 B per K16 step inside the 128 B swizzled row (>>4 => +2)
+                umma_bf16_pair(d_tmem + sub * kSubN, adesc + 2ull * k, bdesc + 2ull * k, idesc,
+                               (kb | sl | k) != 0 ? 1u : 0u);
+              }
             }
           }
           umma_commit_pair(empty_self + stage * 8u);
@@ -307,16 +319,19 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     __syncwarp();
   } else {
     // ----------------------------------------------------------- epilogue
-    const int quarter = warp & 3;   // TMEM lanes this warp may read
-    const int ew = warp - 2;        // staging-buffer owner index
-    const uint32_t my_store = store_base + ew * 2 * kStoreBufBytes;
+    // Warp w reads TMEM lane quarter w % 4 (hardware rule) of sub-tile
+    // (w - 2) / 4: 32 rows x 256 columns per tile.
+    const int quarter = warp & 3;
+    const int ew = warp - 2;
+    const int sub = ew >> 2;
+    const uint32_t my_store = store_base + ew * P::kStoreBufs * kStoreBufBytes;
     const uint32_t acc_empty_leader = cluster_map(smem_u32(&bar_acc_empty[0]), 0);
     uint32_t nstore = 0;
     int it = 0;
     for (int t = pair; t < tiles; t += npairs, ++it) {
       int tm, tn;
       tile_coord(t, args.tiles_m, args.tiles_n, args.group, &tm, &tn);
-      const uint32_t buf = it & 1, acc_phase = (it >> 1) & 1;
+      const uint32_t buf = it % kAccBufs, acc_phase = (it / kAccBufs) & 1;
       if constexpr (kProfile) {
         if (lane == 0) prof.start(kTagWaitMainloop);
       }
@@ -330,50 +345,77 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       if constexpr (kProfile) {
         if (lane == 0) { prof.stop(); prof.start(kTagEpilogue); }
       }
-      const uint32_t tbase = tmem_base + buf * kPairN + ((uint32_t)(quarter * 32) << 16);
+      const uint32_t tbase =
+          tmem_base + buf * P::kTileN + sub * kSubN + ((uint32_t)(quarter * 32) << 16);
       const int row0 = tm * kPairM + (int)rank * kCtaM + quarter * 32;
-      const int col0 = tn * kPairN;
+      const int col0 = tn * P::kTileN + sub * kSubN;
+      // Row `lane` of a 32x64 box is 8 chunks of 16 B; chunk j is stored at
+      // position j ^ (row % 8) -- the TMA 128 B swizzle pattern.
+      const uint32_t row_off = lane * 128u;
+      if constexpr (kNSub == 1) {
 #pragma unroll 1
-      for (int c = 0; c < kPairN / kStoreCols; ++c) {
-        uint32_t v0[32], v1[32];
-        tmem_ld_32x32b_x32(tbase + c * kStoreCols, v0);
-        tmem_ld_32x32b_x32(tbase + c * kStoreCols + 32, v1);
-        tmem_wait_ld();
-        if (c == kPairN / kStoreCols - 1) {
-          // All of this buffer is in registers: hand TMEM back to the MMA.
-          tc_fence_before_sync();
+        for (int c = 0; c < kSubN / kStoreCols; ++c) {
+          uint32_t v0[32], v1[32];
+          tmem_ld_32x32b_x32(tbase + c * kStoreCols, v0);
+          tmem_ld_32x32b_x32(tbase + c * kStoreCols + 32, v1);
+          tmem_wait_ld();
+          if (c == kSubN / kStoreCols - 1) {
+            // All of this warp's part of the buffer is in registers: hand
+            // TMEM back to the MMA.
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc_empty_leader + buf * 8u);
+          }
+          const uint32_t sb = my_store + (nstore & 1u) * kStoreBufBytes;
+          if (lane == 0) bulk_wait_group_read<1>();  // the store that last used sb has read it
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(acc_empty_leader + buf * 8u);
-        }
-        const uint32_t sb = my_store + (nstore & 1u) * kStoreBufBytes;
-        if (lane == 0) bulk_wait_group_read<1>();  // the store that last used sb has read it
-        __syncwarp();
-        // Row `lane` of the 32x64 box: 8 chunks of 16 B, chunk j stored at
-        // position j ^ (row % 8) -- the TMA 128 B swizzle pattern.
-        const uint32_t row_addr = sb + lane * 128u;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          st_shared_v4(row_addr + ((uint32_t)(j ^ (lane & 7)) << 4),
-                       pack_bf16x2(v0[8 * j + 0], v0[8 * j + 1]),
-                       pack_bf16x2(v0[8 * j + 2], v0[8 * j + 3]),
-                       pack_bf16x2(v0[8 * j + 4], v0[8 * j + 5]),
-                       pack_bf16x2(v0[8 * j + 6], v0[8 * j + 7]));
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t* v = j < 4 ? v0 + 8 * j : v1 + 8 * (j - 4);
+            st_shared_v4(sb + row_off + ((uint32_t)(j ^ (lane & 7)) << 4),
+                         pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                         pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_c, sb, col0 + c * kStoreCols, row0);
+            bulk_commit_group();
+          }
+          ++nstore;
         }
+      } else {
+        // Drain this warp's 32 x 256 slice into registers as packed bf16
+        // (128 registers per thread), release the accumulator, then store.
+        uint32_t packed[kSubN / 2];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          st_shared_v4(row_addr + ((uint32_t)((j + 4) ^ (lane & 7)) << 4),
-                       pack_bf16x2(v1[8 * j + 0], v1[8 * j + 1]),
-                       pack_bf16x2(v1[8 * j + 2], v1[8 * j + 3]),
-                       pack_bf16x2(v1[8 * j + 4], v1[8 * j + 5]),
-                       pack_bf16x2(v1[8 * j + 6], v1[8 * j + 7]));
+        for (int c = 0; c < kSubN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) packed[c * 16 + i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
         }
-        fence_proxy_async_smem();
+        tc_fence_before_sync();
         __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmap_c, sb, col0 + c * kStoreCols, row0);
-          bulk_commit_group();
+        if (lane == 0) mbar_arrive_cluster(acc_empty_leader + buf * 8u);
+#pragma unroll
+        for (int c = 0; c < kSubN / kStoreCols; ++c) {
+          if (lane == 0) bulk_wait_group_read<0>();  // the single buffer is free again
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t* p = packed + c * 32 + 4 * j;
+            st_shared_v4(my_store + row_off + ((uint32_t)(j ^ (lane & 7)) << 4), p[0], p[1],
+                         p[2], p[3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_c, my_store, col0 + c * kStoreCols, row0);
+            bulk_commit_group();
+          }
         }
-        ++nstore;
       }
       if constexpr (kProfile) {
         if (lane == 0) prof.stop();

@@ -4,12 +4,12 @@
 // the CPU tests can check it through the C-ABI without a GPU.
 //
 // Geometry (one 2-CTA cluster = one "pair"):
-//   pair tile        256 (M) x 256 (N), K stepped in blocks of 64
-//   per CTA          128 rows of A and 128 rows of B (its half of the N tile)
+//   pair tile        256 (M) x 256 or 512 (N), K stepped in blocks of 64/128
+//   per CTA          128 rows of A and, per 256-wide N sub-tile, 128 rows of
+//                    B (its half of the sub-tile)
 //   MMA              tcgen05.mma.cta_group::2.kind::f16, M=256 N=256 K=16
-//   accumulator      fp32 in TMEM, 128 lanes x 256 columns per CTA, two
-//                    buffers (512 columns) so the epilogue of tile i
-//                    overlaps the main loop of tile i+1
+//   accumulator      fp32 in TMEM, 128 lanes x 256 columns per CTA per
+//                    sub-tile; 512 columns in all
 // The reference computes the same 256x256 cluster tile with BK=64
 // (kernel_v8.cu:775-833, launch_matmul_v8<128, 256, 64>).
 #pragma once
@@ -24,36 +24,50 @@
 namespace b200 {
 
 constexpr int kPairM = 256;        // rows of C per pair tile
-constexpr int kPairN = 256;        // columns of C per pair tile
+constexpr int kSubN = 256;         // columns of one N sub-tile (= MMA N)
 constexpr int kCtaM = 128;         // rows of A (and of C) owned by one CTA
-constexpr int kCtaN = 128;         // rows of B loaded by one CTA
+constexpr int kCtaN = 128;         // rows of B per sub-tile loaded by one CTA
 constexpr int kSlabK = 64;         // K elements per 128 B swizzle slab (one TMA box)
 constexpr int kSlabBytes = 128 * kSlabK * 2;   // 16 KiB: one 128-row operand slab
 constexpr int kMmaK = 16;          // K per tcgen05.mma kind::f16
-constexpr int kAccBufs = 2;        // TMEM accumulator buffers
-constexpr int kTmemCols = kAccBufs * kPairN;   // 512 = the whole TMEM of an SM
+constexpr int kTmemCols = 512;     // the whole TMEM of an SM
 constexpr int kStoreCols = 64;     // epilogue chunk width (one 128 B swizzle row of bf16)
-constexpr int kEpiWarps = 4;       // epilogue warps (one per TMEM lane quarter)
-constexpr int kWarps = 2 + kEpiWarps;          // producer, MMA, 4 x epilogue
-constexpr int kThreads = kWarps * 32;
 constexpr int kStoreBufBytes = 32 * kStoreCols * 2;        // 4 KiB: 32 rows x 64 columns
-constexpr int kStoreBytes = kEpiWarps * 2 * kStoreBufBytes; // 2 buffers per epilogue warp
 constexpr int kSmemBudget = 227 * 1024;                    // opt-in shared memory per CTA
 constexpr int kSmemReserve = 1024 + 1024;                  // 1 KiB alignment + static/barriers
 
-// Pipeline shape for a K block of kSlabs x 64 elements per stage.  A stage
-// holds kSlabs slabs of A then kSlabs slabs of B (16 KiB each, 1 KiB
-// aligned); the ring depth is whatever fits beside the epilogue staging.
-// Fewer, deeper stages mean fewer barrier round trips and tcgen05.commits per
-// MMA; more stages mean finer-grained slot recycling.
-template <int kSlabs>
-struct Pipe {
+// Kernel configuration.
+//   kSlabs  K slabs of 64 per pipeline stage (stage K = 64 * kSlabs)
+//   kNSub   256-wide N sub-tiles per pair tile: 1 -> 256 x 256 pair tiles with
+//           two TMEM accumulators (epilogue of tile i overlaps the MMAs of
+//           tile i+1); 2 -> 256 x 512 pair tiles with one 512-column
+//           accumulator, where each A slab feeds two MMAs, so 25% fewer
+//           operand bytes cross L2 per FLOP, at the cost of the MMA waiting
+//           for the epilogue to drain TMEM once per tile.
+// A stage holds kSlabs slabs of A, then kNSub x kSlabs slabs of B (16 KiB
+// each, 1 KiB aligned); the ring depth is whatever fits beside the epilogue
+// staging buffers.
+template <int kSlabs, int kNSub>
+struct Cfg {
+  static constexpr int kTileN = kNSub * kSubN;
+  static constexpr int kAccBufs = kNSub == 1 ? 2 : 1;
+  static constexpr int kEpiWarps = 4 * kNSub;          // one per (lane quarter, sub-tile)
+  static constexpr int kWarps = 2 + kEpiWarps;         // producer, MMA, epilogue
+  static constexpr int kThreads = 32 * kWarps;
   static constexpr int kBK = kSlabs * kSlabK;
   static constexpr int kBytesA = kSlabs * kSlabBytes;
-  static constexpr int kStageBytes = 2 * kBytesA;
+  static constexpr int kBytesB = kNSub * kSlabs * kSlabBytes;
+  static constexpr int kStageBytes = kBytesA + kBytesB;
+  // 256-wide tiles: two staging buffers per epilogue warp, so storing chunk
+  // c overlaps converting chunk c+1.  512-wide tiles: the epilogue first
+  // moves its whole TMEM slice into registers (as packed bf16) to free the
+  // single accumulator early, then stores from registers through one buffer.
+  static constexpr int kStoreBufs = kNSub == 1 ? 2 : 1;
+  static constexpr int kStoreBytes = kEpiWarps * kStoreBufs * kStoreBufBytes;
   static constexpr int kStages = (kSmemBudget - kStoreBytes - kSmemReserve) / kStageBytes;
   static constexpr int kSmemBytes = kStages * kStageBytes + kStoreBytes + 1024;
   static_assert(kStages >= 2, "pipeline needs at least two stages");
+  static_assert(kAccBufs * kTileN <= kTmemCols, "accumulators exceed TMEM");
 };
 
 // ---------------------------------------------------------------------------

@@ -47,7 +47,8 @@ int b200_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, i
 
 /* Same GEMM with the intra-kernel profiler on.  `profiler` is a device int64
  * buffer of rows x (1 + 4 * num_entries) entries, rows from
- * b200_gemm_profile_rows; row r = block * 6 + warp holds
+ * b200_gemm_profile_rows; row r = block * warps_per_cta + warp (warps per
+ * CTA = threads from b200_gemm_launch_shape / 32) holds
  * [count, (smid, tag, start_ns, duration_ns) x count].  Writes past a row's
  * capacity are dropped.
  * Replaces profile_matmul_v5 ... profile_matmul_v8 (src/matmul.cpp:16-23). */
@@ -66,14 +67,19 @@ int b200_gemm_profile_rows(int M, int N, int K, int* rows);
  * counterpart (the reference's waits never give up, kernel_v8.cu:60-76). */
 int b200_gemm_device_status(int clear, int* status_out);
 
-/* Process-wide tuning: K slabs of 64 per pipeline stage (1: 6 stages of
- * K=64, 2: 3 stages of K=128) and the band width, in 256-wide tiles, of the
- * persistent raster (positive: bands of tile-rows, negative: bands of
- * tile-columns).  0 keeps a value.  Defaults come from B200_GEMM_SLABS /
- * B200_GEMM_GROUP.  Plays the role of the reference's GEMM_L2_A/GEMM_L2_B
- * environment knobs (src/kernels/kernel_v8.cu:11-31). */
-int b200_gemm_set_tuning(int stage_slabs, int raster_group);
-int b200_gemm_get_tuning(int* stage_slabs, int* raster_group);
+/* Process-wide tuning.
+ *   tile_n        pair-tile width: 256 (two TMEM accumulators, epilogue
+ *                 overlapped), 512 (one A slab feeds two MMAs: 25% fewer
+ *                 operand bytes per FLOP) or -1 to choose per shape; 0 keeps
+ *   stage_slabs   K slabs of 64 per stage for 256-wide tiles (1: 6 stages of
+ *                 K=64, 2: 3 stages of K=128); 0 keeps
+ *   raster_group  band width, in tiles, of the persistent raster (positive:
+ *                 bands of tile-rows, negative: bands of tile-columns); 0 keeps
+ * Defaults come from B200_GEMM_TILE_N / B200_GEMM_SLABS / B200_GEMM_GROUP.
+ * Plays the role of the reference's GEMM_L2_A/GEMM_L2_B environment knobs
+ * (src/kernels/kernel_v8.cu:11-31). */
+int b200_gemm_set_tuning(int tile_n, int stage_slabs, int raster_group);
+int b200_gemm_get_tuning(int* tile_n, int* stage_slabs, int* raster_group);
 
 /* Upper bound, in nanoseconds, on any single pipeline wait inside the GEMM
  * kernels of this process (default 2 s).  No reference counterpart. */

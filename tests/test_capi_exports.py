@@ -73,6 +73,18 @@ def test_profile_requires_buffer():
     assert st == capi.ERR_INVALID_ARGUMENT
 
 
+def test_tuning_roundtrip_and_validation():
+    before = capi.get_tuning()
+    capi.set_tuning(512, 2, -4)
+    assert capi.get_tuning() == {"tile_n": 512, "stage_slabs": 2, "raster_group": -4}
+    capi.set_tuning(-1, 1, -8)
+    assert capi.get_tuning()["tile_n"] == 0
+    for bad in ((300, 0, 0), (0, 3, 0), (0, -1, 0)):
+        with pytest.raises(capi.GemmError):
+            capi.set_tuning(*bad)
+    capi.set_tuning(before["tile_n"] or -1, before["stage_slabs"], before["raster_group"])
+
+
 def test_timeout_setter_rejects_zero():
     with pytest.raises(capi.GemmError):
         capi.set_wait_timeout_ns(0)

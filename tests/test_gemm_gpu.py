@@ -60,12 +60,17 @@ def within_tol(C, R, A, Bt, rows=None):
     return m
 
 
-@pytest.fixture(autouse=True, params=[1, 2], ids=["bk64x6", "bk128x3"])
-def pipeline(request):
-    """Every test runs on both pipeline shapes of the kernel."""
-    capi.set_tuning(request.param, 8)
+CONFIGS = {"n256_bk64": (256, 1), "n256_bk128": (256, 2), "n512_bk64": (512, 1)}
+
+
+@pytest.fixture(autouse=True, params=list(CONFIGS), ids=list(CONFIGS))
+def kernel_config(request):
+    """Every test runs on every kernel configuration (pair-tile width and
+    stage depth), forced regardless of the per-shape choice."""
+    tile_n, slabs = CONFIGS[request.param]
+    capi.set_tuning(tile_n, slabs, 0)
     yield request.param
-    capi.set_tuning(1, 8)
+    capi.set_tuning(-1, 1, 0)
 
 
 # ------------------------------------------------------------ small shapes
@@ -288,11 +293,12 @@ def test_profiler_variant_matches_and_records():
     C0 = bg.matmul_b200(A, Bt.T)
     torch.cuda.synchronize()
     assert torch.equal(C.view(torch.int16), C0.view(torch.int16))
-    ev = list(profiler.decode(buf))
+    warps = profiler.warps_per_cta(M, N, K)
+    ev = list(profiler.decode(buf, warps))
     tags = {e["tag"] for e in ev}
     assert {"Setup", "IssueTMA", "IssueMMA", "Epilogue"} <= tags
     assert all(e["dur_ns"] >= 0 for e in ev)
-    s = profiler.summary(buf)
+    s = profiler.summary(buf, warps)
     assert s["span_ns"] > 0
     # a tiny capacity must truncate, never overrun
     buf2 = profiler.alloc(M, N, K, 2)

@@ -103,11 +103,22 @@ def test_persistent_assignment_covers_all_tiles_once():
 
 
 def test_launch_shape_without_gpu():
-    s = capi.launch_shape(8192, 8192, 8192)
-    assert s["tiles"] == 32 * 32
-    assert s["threads"] == 192
-    assert s["smem_bytes"] <= 227 * 1024
-    s = capi.launch_shape(16, 8192, 8192)
-    assert s["tiles"] == 32
-    s = capi.launch_shape(300, 520, 200)
-    assert s["tiles"] == 2 * 3
+    before = capi.get_tuning()
+    try:
+        capi.set_tuning(256, 1, 0)
+        s = capi.launch_shape(8192, 8192, 8192)
+        assert s["tiles"] == 32 * 32 and s["threads"] == 192
+        assert s["smem_bytes"] <= 227 * 1024
+        assert capi.launch_shape(16, 8192, 8192)["tiles"] == 32
+        assert capi.launch_shape(300, 520, 200)["tiles"] == 2 * 3
+        capi.set_tuning(512, 1, 0)
+        s = capi.launch_shape(8192, 8192, 8192)
+        assert s["tiles"] == 32 * 16 and s["threads"] == 320
+        assert s["smem_bytes"] <= 227 * 1024
+        capi.set_tuning(-1, 1, 0)
+        # per-shape choice: wide tiles on a big grid, 256-wide on a small one
+        assert capi.launch_shape(8192, 8192, 8192)["threads"] == 320
+        assert capi.launch_shape(2048, 2048, 2048)["threads"] == 192
+        assert capi.launch_shape(16, 8192, 8192)["threads"] == 192
+    finally:
+        capi.set_tuning(before["tile_n"] or -1, before["stage_slabs"], before["raster_group"])
