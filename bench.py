@@ -41,6 +41,11 @@ sys.path.insert(0, str(ROOT))
 M_PER_GPU, N_DIM, K_DIM = 8192, 8192, 8192
 FLUSH_BYTES = 256 * 1024 * 1024
 FALLBACK_BF16_TFLOPS = 1590.0      # earlier measurement on this pool (burst)
+# Every timed arm (ours, cuBLAS, the reference) starts after the GPU has
+# idled this long, so each sees the same power-limiter state; the reference
+# harness gets the same by running each (shape, version) in a fresh
+# container (src/main.py:85-100,158).
+IDLE_BEFORE_ARM_S = 1.0
 
 
 # --------------------------------------------------------------- utilities
@@ -131,6 +136,14 @@ class ClockSampler:
         return out
 
 
+def step_stats(ms):
+    """Distribution of the per-step GEMM times of one rank (ms)."""
+    k = max(1, len(ms) // 10)
+    return {"min": min(ms), "median": statistics.median(ms), "mean": statistics.mean(ms),
+            "max": max(ms), "first_tenth_mean": statistics.mean(ms[:k]),
+            "last_tenth_mean": statistics.mean(ms[-k:])}
+
+
 def cold_l2_loop(fn, steps, stream, flush):
     """Per step: write the flush buffer, then time fn() with events."""
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -144,6 +157,8 @@ def cold_l2_loop(fn, steps, stream, flush):
 
 
 def time_cold(fn, steps, warmup, stream, flush):
+    torch.cuda.synchronize()
+    time.sleep(IDLE_BEFORE_ARM_S)
     for _ in range(warmup):
         flush.zero_()
         fn()
@@ -278,6 +293,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     import blackwell_gemm_b200  # noqa: F401  (loads the native library; fails loudly)
+    from blackwell_gemm_b200 import capi
     from blackwell_gemm_b200.workloads import make_operands
 
     M, N, K = M_PER_GPU, N_DIM, K_DIM
@@ -290,7 +306,11 @@ def main():
     gemm_ours(A, Bt, C, stream)
     torch.cuda.synchronize()
     par = parity_sample(C, A, Bt)
+    tuning = capi.get_tuning()
+    shape = capi.launch_shape(M, N, K)
 
+    torch.cuda.synchronize()
+    time.sleep(IDLE_BEFORE_ARM_S)
     for _ in range(args.warmup):
         flush.zero_()
         gemm_ours(A, Bt, C, stream)
@@ -356,13 +376,14 @@ def main():
         except Exception as e:  # the reference build may be absent
             extras["reference_v8_error"] = repr(e)
         cub_ms = statistics.median(time_cold(lambda: torch.matmul(A, Bt.T), 50, 10, stream, flush))
-        ours_med = statistics.median(launch_ms)
+        ours_med = statistics.median(time_cold(lambda: gemm_ours(A, Bt, C, stream), 50, 10, stream,
+                                               flush))
         extras["baselines"] = {
             "ours_median_tflops": flops_step / (ours_med * 1e-3) / 1e12,
             "cublas_median_tflops": flops_step / (cub_ms * 1e-3) / 1e12,
             "reference_v8_median_tflops": (flops_step / (ref_ms * 1e-3) / 1e12) if ref_ms else None,
-            "method": "median of 50 cold-L2 launches each, same process and inputs "
-                      "(src/bench_core.py:47-69 method)"}
+            "method": "median of 50 cold-L2 launches each after 1 s idle and 10 warm-up "
+                      "launches, same process and inputs (src/bench_core.py:47-69 method)"}
         extras["cpu_baseline"] = cpu_baseline(Bt)
 
     if rank == 0:
@@ -378,12 +399,16 @@ def main():
                        "l2": "flushed: 256 MB written before every step, outside the GEMM events",
                        "parallelism": f"m-shard{world}"},
             "timed_region_ms": region_ms_max,
+            "step_ms": step_stats(launch_ms),
             "gpu_launches": args.steps,
             "roofline": roofline,
             "e2e": e2e,
             "clocks": clocks.report(),
             "parity": par,
             "impl": "ours",
+            "kernel": {"pair_tile": "256x512" if shape["threads"] // 32 > 6 else "256x256",
+                       "threads": shape["threads"], "grid": shape["grid"],
+                       "smem_bytes": shape["smem_bytes"], "tuning": tuning},
         }
         line.update(extras)
         print(json.dumps(line), flush=True)
@@ -417,6 +442,8 @@ def run_reference(args, world, rank, dev):
     gemm_reference(A, Bt, C, stream)
     torch.cuda.synchronize()
     par = parity_sample(C, A, Bt)
+    torch.cuda.synchronize()
+    time.sleep(IDLE_BEFORE_ARM_S)
     for _ in range(args.warmup):
         flush.zero_()
         gemm_reference(A, Bt, C, stream)
@@ -450,6 +477,7 @@ def run_reference(args, world, rank, dev):
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e_ms,
                 "path": "reference matmul_v8 launcher with pinned host A, B and C"},
         "gpu_launches": 0,
+        "step_ms": step_stats(launch_ms),
         "clocks": clocks.report(),
         "parity": par,
     }
