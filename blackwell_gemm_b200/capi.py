@@ -38,6 +38,10 @@ _ip = ctypes.POINTER(ctypes.c_int)
 SIGNATURES = {
     "b200_gemm_bf16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "b200_gemm_bf16_profile": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp]),
+    "b200_gemm_bf16_f32out": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "b200_cast_f32_bf16": (_i, [_vp, _i, _vp, _i, _i, _i, _vp]),
+    "b200_gemm_set_splits": (_i, [_i]),
+    "b200_gemm_get_splits": (_i, [_i, _i, _i, _ip]),
     "b200_gemm_profile_rows": (_i, [_i, _i, _i, _ip]),
     "b200_gemm_device_status": (_i, [_i, _ip]),
     "b200_gemm_set_wait_timeout_ns": (_i, [_ull]),
@@ -87,6 +91,27 @@ def gemm_bf16(a_ptr: int, b_ptr: int, c_ptr: int, M: int, N: int, K: int, lda: i
               ldc: int, stream: int = 0) -> int:
     """Raw C-ABI call: returns the status code (does not raise)."""
     return lib().b200_gemm_bf16(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, stream)
+
+
+def gemm_bf16_f32out(a_ptr: int, b_ptr: int, c_ptr: int, M: int, N: int, K: int, lda: int,
+                     ldb: int, ldc: int, stream: int = 0) -> int:
+    """fp32 C = A * B^T (no rounding); ldc in floats.  Returns the status."""
+    return lib().b200_gemm_bf16_f32out(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, stream)
+
+
+def cast_f32_bf16(w_ptr: int, ldw: int, c_ptr: int, ldc: int, M: int, N: int,
+                  stream: int = 0) -> int:
+    return lib().b200_cast_f32_bf16(w_ptr, ldw, c_ptr, ldc, M, N, stream)
+
+
+def set_splits(splits: int) -> None:
+    check(lib().b200_gemm_set_splits(int(splits)), "set_splits")
+
+
+def get_splits(M: int, N: int, K: int) -> int:
+    v = ctypes.c_int(0)
+    check(lib().b200_gemm_get_splits(M, N, K, ctypes.byref(v)), "get_splits")
+    return v.value
 
 
 def gemm_bf16_profile(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, prof_ptr, entries,

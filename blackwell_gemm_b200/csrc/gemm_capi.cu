@@ -62,6 +62,7 @@ struct DeviceState {
   int sms = 0;
   int max_pairs[kNumVariants] = {0, 0, 0};  // co-resident 2-CTA clusters per variant
   int* status = nullptr;                    // device error word
+  cudaMemPool_t pool = nullptr;             // stream-ordered split-K workspaces
 };
 
 std::mutex g_mu;
@@ -82,6 +83,17 @@ int env_int(const char* name, int fallback, int lo, int hi) {
 std::atomic<int> g_tile_n{-1};
 std::atomic<int> g_slabs{-1};
 std::atomic<int> g_group{0};
+std::atomic<int> g_splits{-1};
+
+// Split-K slices: 0 = chosen per shape, 1 = never split, n = n slices.
+int tuning_splits() {
+  int v = g_splits.load();
+  if (v < 0) {
+    v = env_int("B200_GEMM_SPLITS", 0, 0, 64);
+    g_splits.store(v);
+  }
+  return v;
+}
 
 int tuning_tile_n() {
   int v = g_tile_n.load();
@@ -127,22 +139,24 @@ int query_pairs(int sms, int* out) {
   cfg.numAttrs = 1;
   int n = 0;
   if (cudaOccupancyMaxActiveClusters(
-          &n, gemm_bf16_pair_kernel<false, kVariantSlabs[V], kVariantNSub[V]>, &cfg) !=
+          &n, gemm_bf16_pair_kernel<false, kVariantSlabs[V], kVariantNSub[V], kOutBf16>, &cfg) !=
       cudaSuccess)
     return B200_ERR_LAUNCH;
   *out = n;
   return B200_OK;
 }
 
+template <bool kProfile, int V, int kOut>
+bool set_smem_limit() {
+  return cudaFuncSetAttribute(
+             gemm_bf16_pair_kernel<kProfile, kVariantSlabs[V], kVariantNSub[V], kOut>,
+             cudaFuncAttributeMaxDynamicSharedMemorySize, VariantCfg<V>::C::kSmemBytes) ==
+         cudaSuccess;
+}
+
 template <int V>
 bool set_smem_limits() {
-  constexpr int S = kVariantSlabs[V], NS = kVariantNSub[V];
-  constexpr int bytes = VariantCfg<V>::C::kSmemBytes;
-  return cudaFuncSetAttribute(gemm_bf16_pair_kernel<false, S, NS>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
-             cudaSuccess &&
-         cudaFuncSetAttribute(gemm_bf16_pair_kernel<true, S, NS>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
+  return set_smem_limit<false, V, kOutBf16>() && set_smem_limit<true, V, kOutBf16>();
 }
 
 int init_device(DeviceState& d, int dev) {
@@ -152,7 +166,8 @@ int init_device(DeviceState& d, int dev) {
   if (encode_tiled() == nullptr) return B200_ERR_TENSOR_MAP;
   d.sms = prop.multiProcessorCount;
   if (!set_smem_limits<kV256x64>() || !set_smem_limits<kV256x128>() ||
-      !set_smem_limits<kV512x64>())
+      !set_smem_limits<kV512x64>() || !set_smem_limit<false, kV256x64, kOutF32>() ||
+      !set_smem_limit<false, kV256x64, kOutF32Add>())
     return B200_ERR_LAUNCH;
   if (query_pairs<kV256x64>(d.sms, &d.max_pairs[kV256x64]) != B200_OK ||
       query_pairs<kV256x128>(d.sms, &d.max_pairs[kV256x128]) != B200_OK ||
@@ -162,6 +177,17 @@ int init_device(DeviceState& d, int dev) {
     if (d.max_pairs[v] < 1) return B200_ERR_LAUNCH;
   if (cudaMalloc(&d.status, sizeof(int)) != cudaSuccess ||
       cudaMemset(d.status, 0, sizeof(int)) != cudaSuccess)
+    return B200_ERR_LAUNCH;
+  // Split-K workspaces come from a pool of our own, allocated and freed in
+  // stream order, so concurrent calls on different streams never share one;
+  // the pool keeps up to 256 MiB mapped between calls.
+  cudaMemPoolProps props = {};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = dev;
+  if (cudaMemPoolCreate(&d.pool, &props) != cudaSuccess) return B200_ERR_LAUNCH;
+  unsigned long long keep = 256ull << 20;
+  if (cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep) != cudaSuccess)
     return B200_ERR_LAUNCH;
   return B200_OK;
 }
@@ -228,41 +254,93 @@ CUtensorMapL2promotion l2_promotion() {
 }
 
 int encode_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
-              uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+              uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+              bool fp32 = false) {
   const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {row_stride_elems * 2};
+  const cuuint64_t strides[1] = {row_stride_elems * (fp32 ? 4 : 2)};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = encode_tiled()(
-      map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, l2_promotion(),
-      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+      const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      CU_TENSOR_MAP_SWIZZLE_128B, l2_promotion(), CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TENSOR_MAP;
 }
 
 int validate(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
-             int ldc) {
+             int ldc, bool c_fp32 = false) {
   if (M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARGUMENT;
   if (M == 0 || N == 0) return B200_OK;
   if (!C || (K > 0 && (!A || !B))) return B200_ERR_INVALID_ARGUMENT;
   if (ldc < N || (K > 0 && (lda < K || ldb < K))) return B200_ERR_INVALID_ARGUMENT;
-  if (!aligned16(C) || (ldc & 7)) return B200_ERR_ALIGNMENT;
+  if (!aligned16(C) || (ldc & (c_fp32 ? 3 : 7))) return B200_ERR_ALIGNMENT;
   if (K > 0 && (!aligned16(A) || !aligned16(B) || (lda & 7) || (ldb & 7)))
     return B200_ERR_ALIGNMENT;
   return B200_OK;
 }
 
-template <bool kProfile, int V>
+// Slices for split-K.  A grid of fewer 256 x 256 tiles than half the pairs
+// leaves SMs idle (the skinny, HBM-bound shapes), so a deep K is cut into up
+// to 16 slices of at least 8 K-blocks.  Shallow problems (fewer than 32
+// K-blocks, e.g. 1024^3) are not split: the workspace clear and the rounding
+// pass cost more than the idle SMs.
+int choose_splits(long long tiles, int k_blocks, int pairs) {
+  const int forced = tuning_splits();
+  int s;
+  if (forced > 0) {
+    s = forced;
+  } else {
+    if (tiles * 2 > pairs || k_blocks < 32) return 1;
+    s = k_blocks / 8;
+    if (s > 16) s = 16;
+  }
+  if (s > k_blocks) s = k_blocks;
+  return s < 1 ? 1 : s;
+}
+
+template <bool kProfile, int V, int kOut>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmArgs args,
-           const DeviceState& d, cudaStream_t stream) {
+           int splits, const DeviceState& d, cudaStream_t stream) {
   using C = typename VariantCfg<V>::C;
   args.tiles_n = (int)ceil_div(args.N, C::kTileN);
   args.k_blocks = (int)ceil_div(args.K, C::kBK);
-  const long long tiles = (long long)args.tiles_m * args.tiles_n;
-  const int pairs = (int)(tiles < d.max_pairs[V] ? tiles : d.max_pairs[V]);
-  gemm_bf16_pair_kernel<kProfile, kVariantSlabs[V], kVariantNSub[V]>
+  if (splits > args.k_blocks) splits = args.k_blocks;
+  args.kb_per_split = (int)ceil_div(args.k_blocks, splits);
+  args.splits = (int)ceil_div(args.k_blocks, args.kb_per_split);  // every slice non-empty
+  const long long units = (long long)args.tiles_m * args.tiles_n * args.splits;
+  const int pairs = (int)(units < d.max_pairs[V] ? units : d.max_pairs[V]);
+  gemm_bf16_pair_kernel<kProfile, kVariantSlabs[V], kVariantNSub[V], kOut>
       <<<2 * pairs, C::kThreads, C::kSmemBytes, stream>>>(ta, tb, tc, args);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
+}
+
+
+int cast_to_bf16(const float* W, int ldw, void* C, int ldc, int M, int N, int sms,
+                 cudaStream_t stream) {
+  const long long groups = (long long)M * ((N + 7) / 8);
+  long long blocks = ceil_div(groups, 256);
+  if (blocks > 8LL * sms) blocks = 8LL * sms;
+  cast_f32_to_bf16_kernel<<<(int)blocks, 256, 0, stream>>>(
+      W, ldw, static_cast<__nv_bfloat16*>(C), ldc, M, N);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
+}
+
+GemmArgs base_args(int M, int N, int K, const DeviceState& d, long long* prof, int entries) {
+  GemmArgs args;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.tiles_m = (int)ceil_div(M, kPairM);
+  args.tiles_n = 0;
+  args.k_blocks = 0;
+  args.group = raster_group();
+  args.splits = 1;
+  args.kb_per_split = 0;
+  args.status = d.status;
+  args.timeout_ns = g_timeout_ns.load();
+  args.prof = prof;
+  args.prof_entries = entries;
+  return args;
 }
 
 template <bool kProfile>
@@ -287,23 +365,58 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda
       encode_2d(&tc, C, N, M, ldc, kStoreCols, 32) != B200_OK)
     return B200_ERR_TENSOR_MAP;
 
-  GemmArgs args;
-  args.M = M;
-  args.N = N;
-  args.K = K;
-  args.tiles_m = (int)ceil_div(M, kPairM);
-  args.tiles_n = 0;
-  args.k_blocks = 0;
-  args.group = raster_group();
-  args.status = d->status;
-  args.timeout_ns = g_timeout_ns.load();
-  args.prof = prof;
-  args.prof_entries = prof_entries;
-  switch (choose_variant(M, N, d->max_pairs)) {
-    case kV256x128: return launch<kProfile, kV256x128>(ta, tb, tc, args, *d, stream);
-    case kV512x64: return launch<kProfile, kV512x64>(ta, tb, tc, args, *d, stream);
-    default: return launch<kProfile, kV256x64>(ta, tb, tc, args, *d, stream);
+  GemmArgs args = base_args(M, N, K, *d, prof, prof_entries);
+  // Split-K (not with the profiler): tiles accumulate their K slices into a
+  // zeroed fp32 workspace by TMA reduce-add, then one pass rounds to bf16.
+  if (!kProfile) {
+    const long long tiles = ceil_div(M, kPairM) * ceil_div(N, kSubN);
+    const int splits = choose_splits(tiles, (int)ceil_div(K, kSlabK), d->max_pairs[kV256x64]);
+    if (splits > 1) {
+      const int ldw = (int)ceil_div(N, 8) * 8;
+      const size_t bytes = (size_t)M * ldw * sizeof(float);
+      float* W = nullptr;
+      if (cudaMallocFromPoolAsync(reinterpret_cast<void**>(&W), bytes, d->pool, stream) !=
+          cudaSuccess) {
+        cudaGetLastError();
+        return B200_ERR_LAUNCH;
+      }
+      st = encode_2d(&tc, W, N, M, ldw, 32, 32, true);
+      if (st == B200_OK && cudaMemsetAsync(W, 0, bytes, stream) != cudaSuccess)
+        st = B200_ERR_LAUNCH;
+      if (st == B200_OK) st = launch<false, kV256x64, kOutF32Add>(ta, tb, tc, args, splits, *d,
+                                                                   stream);
+      if (st == B200_OK) st = cast_to_bf16(W, ldw, C, ldc, M, N, d->sms, stream);
+      cudaFreeAsync(W, stream);
+      return st;
+    }
   }
+  switch (choose_variant(M, N, d->max_pairs)) {
+    case kV256x128: return launch<kProfile, kV256x128, kOutBf16>(ta, tb, tc, args, 1, *d, stream);
+    case kV512x64: return launch<kProfile, kV512x64, kOutBf16>(ta, tb, tc, args, 1, *d, stream);
+    default: return launch<kProfile, kV256x64, kOutBf16>(ta, tb, tc, args, 1, *d, stream);
+  }
+}
+
+// fp32 C = A * B^T (no rounding), 256 x 256 tiles: the K-split partials.
+int run_gemm_f32out(const void* A, const void* B, float* C, int M, int N, int K, int lda,
+                    int ldb, int ldc, cudaStream_t stream) {
+  int st = validate(A, B, C, M, N, K, lda, ldb, ldc, true);
+  if (st != B200_OK) return st;
+  if (M == 0 || N == 0) return B200_OK;
+  DeviceState* d = nullptr;
+  st = device_state(&d);
+  if (st != B200_OK) return st;
+  if (K == 0)
+    return cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, M, stream) == cudaSuccess
+               ? B200_OK
+               : B200_ERR_LAUNCH;
+  CUtensorMap ta, tb, tc;
+  if (encode_2d(&ta, A, K, M, lda, kSlabK, kCtaM) != B200_OK ||
+      encode_2d(&tb, B, K, N, ldb, kSlabK, kCtaN) != B200_OK ||
+      encode_2d(&tc, C, N, M, ldc, 32, 32, true) != B200_OK)
+    return B200_ERR_TENSOR_MAP;
+  GemmArgs args = base_args(M, N, K, *d, nullptr, 0);
+  return launch<false, kV256x64, kOutF32>(ta, tb, tc, args, 1, *d, stream);
 }
 
 template <int V>
@@ -328,6 +441,22 @@ int b200_gemm_bf16_profile(const void* A, const void* B, void* C, int M, int N, 
                            int ldb, int ldc, int64_t* profiler, int num_entries, void* stream) {
   return run_gemm<true>(A, B, C, M, N, K, lda, ldb, ldc, reinterpret_cast<long long*>(profiler),
                         num_entries, static_cast<cudaStream_t>(stream));
+}
+
+int b200_gemm_bf16_f32out(const void* A, const void* B, float* C, int M, int N, int K, int lda,
+                          int ldb, int ldc, void* stream) {
+  return run_gemm_f32out(A, B, C, M, N, K, lda, ldb, ldc, static_cast<cudaStream_t>(stream));
+}
+
+int b200_cast_f32_bf16(const float* W, int ldw, void* C, int ldc, int M, int N, void* stream) {
+  if (M < 0 || N < 0 || ldw < N || ldc < N) return B200_ERR_INVALID_ARGUMENT;
+  if (M == 0 || N == 0) return B200_OK;
+  if (!W || !C) return B200_ERR_INVALID_ARGUMENT;
+  if (!aligned16(W) || !aligned16(C) || (ldw & 3) || (ldc & 7)) return B200_ERR_ALIGNMENT;
+  DeviceState* d = nullptr;
+  const int st = device_state(&d);
+  if (st != B200_OK) return st;
+  return cast_to_bf16(W, ldw, C, ldc, M, N, d->sms, static_cast<cudaStream_t>(stream));
 }
 
 int b200_gemm_launch_shape(int M, int N, int K, int* tiles, int* grid, int* smem_bytes,
@@ -384,6 +513,23 @@ int b200_gemm_set_tuning(int tile_n, int stage_slabs, int raster_group) {
   else if (tile_n != 0) g_tile_n.store(tile_n);
   if (stage_slabs > 0) g_slabs.store(stage_slabs);
   if (raster_group != 0) g_group.store(raster_group);
+  return B200_OK;
+}
+
+int b200_gemm_set_splits(int splits) {
+  if (splits < 0 || splits > 64) return B200_ERR_INVALID_ARGUMENT;
+  g_splits.store(splits);
+  return B200_OK;
+}
+
+int b200_gemm_get_splits(int M, int N, int K, int* splits) {
+  if (!splits || M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARGUMENT;
+  DeviceState* d = nullptr;
+  const int pairs = device_state(&d) == B200_OK ? d->max_pairs[kV256x64] : 74;
+  *splits = (M == 0 || N == 0 || K == 0)
+                ? 1
+                : choose_splits(ceil_div(M, kPairM) * ceil_div(N, kSubN),
+                                (int)ceil_div(K, kSlabK), pairs);
   return B200_OK;
 }
 

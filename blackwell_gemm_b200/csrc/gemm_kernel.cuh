@@ -39,6 +39,8 @@ namespace b200 {
 struct GemmArgs {
   int M, N, K;
   int tiles_m, tiles_n, k_blocks, group;
+  int splits;        // K slices per tile (split-K); 1 = whole K per tile
+  int kb_per_split;  // K blocks per slice (the last slice may be shorter)
   int* status;                    // device error word (0 = ok)
   unsigned long long timeout_ns;  // bound on any single pipeline wait
   long long* prof;                // intra-kernel profiler rows (nullptr: off)
@@ -137,18 +139,30 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, cons
   return wait_slow(bar, parity, w, code, true);
 }
 
+// Work unit u -> tile (tm, tn) and its K-block range [kb0, kb1).
+__device__ __forceinline__ void unit_coord(int u, const GemmArgs& a, int* tm, int* tn, int* kb0,
+                                           int* kb1) {
+  const int t = u / a.splits;
+  const int s = u - t * a.splits;
+  tile_coord(t, a.tiles_m, a.tiles_n, a.group, tm, tn);
+  *kb0 = s * a.kb_per_split;
+  const int end = *kb0 + a.kb_per_split;
+  *kb1 = end < a.k_blocks ? end : a.k_blocks;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(lo), __uint_as_float(hi));
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <bool kProfile, int kSlabs, int kNSub>
+template <bool kProfile, int kSlabs, int kNSub, int kOut>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<kSlabs, kNSub>::kThreads, 1)
 gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_c,
                       const GemmArgs args) {
   using P = Cfg<kSlabs, kNSub>;
+  static_assert(kOut == kOutBf16 || kNSub == 1, "fp32 outputs use 256-wide pair tiles");
   constexpr int kStages = P::kStages;
   constexpr int kAccBufs = P::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
@@ -165,7 +179,8 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
-  const int tiles = args.tiles_m * args.tiles_n;
+  // Work units: (tile, K slice) pairs, unit u = tile * splits + slice.
+  const int units = args.tiles_m * args.tiles_n * args.splits;
 
   // 1 KiB aligned start: the 128 B swizzle atoms (8 rows x 128 B) must be.
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -222,12 +237,12 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       uint32_t stage = 0, phase = 0;
       uint32_t filled = 0;  // ring slots this producer has filled so far
       bool ok = true;
-      for (int t = pair; ok && t < tiles; t += npairs) {
-        int tm, tn;
-        tile_coord(t, args.tiles_m, args.tiles_n, args.group, &tm, &tn);
+      for (int u = pair; ok && u < units; u += npairs) {
+        int tm, tn, kb0, kb1;
+        unit_coord(u, args, &tm, &tn, &kb0, &kb1);
         const int a_row = tm * kPairM + (int)rank * kCtaM;
         const int b_row = tn * P::kTileN + (int)rank * kCtaN;
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if constexpr (kProfile) prof.start(kTagWaitMMA);
           if (!wait_bounded(smem_u32(&bar_empty[stage]), phase ^ 1u, wctx, kErrWaitEmpty)) {
             ok = false;
@@ -268,7 +283,9 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       uint32_t stage = 0, phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = pair; ok && t < tiles; t += npairs, ++it) {
+      for (int u = pair; ok && u < units; u += npairs, ++it) {
+        int tm, tn, kb0, kb1;
+        unit_coord(u, args, &tm, &tn, &kb0, &kb1);
         const uint32_t buf = it % kAccBufs, acc_phase = (it / kAccBufs) & 1;
         if constexpr (kProfile) prof.start(kTagWaitEpilogue);
         if (!wait_bounded(smem_u32(&bar_acc_empty[buf]), acc_phase ^ 1u, wctx, kErrWaitAccEmpty))
@@ -276,7 +293,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
         if constexpr (kProfile) prof.stop();
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + buf * P::kTileN;
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if constexpr (kProfile) prof.start(kTagWaitTMA);
           if (!wait_bounded(smem_u32(&bar_full[stage]), phase, wctx, kErrWaitFull)) {
             ok = false;
@@ -296,7 +313,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     make_sdesc_k128(sa + P::kBytesA + (sub * kSlabs + sl) * kSlabBytes);
                 // +32 B per K16 step inside the 128 B swizzled row (>>4 => +2)
                 umma_bf16_pair(d_tmem + sub * kSubN, adesc + 2ull * k, bdesc + 2ull * k, idesc,
-                               (kb | sl | k) != 0 ? 1u : 0u);
+                               (kb != kb0 || sl != 0 || k != 0) ? 1u : 0u);
               }
             }
           }
@@ -328,9 +345,9 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const uint32_t acc_empty_leader = cluster_map(smem_u32(&bar_acc_empty[0]), 0);
     uint32_t nstore = 0;
     int it = 0;
-    for (int t = pair; t < tiles; t += npairs, ++it) {
-      int tm, tn;
-      tile_coord(t, args.tiles_m, args.tiles_n, args.group, &tm, &tn);
+    for (int u = pair; u < units; u += npairs, ++it) {
+      int tm, tn, kb0, kb1;
+      unit_coord(u, args, &tm, &tn, &kb0, &kb1);
       const uint32_t buf = it % kAccBufs, acc_phase = (it / kAccBufs) & 1;
       if constexpr (kProfile) {
         if (lane == 0) prof.start(kTagWaitMainloop);
@@ -352,7 +369,38 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       // Row `lane` of a 32x64 box is 8 chunks of 16 B; chunk j is stored at
       // position j ^ (row % 8) -- the TMA 128 B swizzle pattern.
       const uint32_t row_off = lane * 128u;
-      if constexpr (kNSub == 1) {
+      if constexpr (kOut != kOutBf16) {
+        // fp32: 8 chunks of 32 columns (128 B rows); chunk j of 16 B at
+        // position j ^ (row % 8), as above.
+#pragma unroll 1
+        for (int c = 0; c < kSubN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, v);
+          tmem_wait_ld();
+          if (c == kSubN / 32 - 1) {
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc_empty_leader + buf * 8u);
+          }
+          const uint32_t sb = my_store + (nstore & 1u) * kStoreBufBytes;
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            st_shared_v4(sb + row_off + ((uint32_t)(j ^ (lane & 7)) << 4), v[4 * j],
+                         v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (kOut == kOutF32Add)
+              tma_reduce_add_2d(&tmap_c, sb, col0 + c * 32, row0);
+            else
+              tma_store_2d(&tmap_c, sb, col0 + c * 32, row0);
+            bulk_commit_group();
+          }
+          ++nstore;
+        }
+      } else if constexpr (kNSub == 1) {
 #pragma unroll 1
         for (int c = 0; c < kSubN / kStoreCols; ++c) {
           uint32_t v0[32], v1[32];
@@ -460,6 +508,36 @@ __global__ void __cluster_dims__(2, 1, 1) wait_probe_kernel(int* status,
     wait_bounded(smem_u32(&bar), 0, w, kErrWaitProbe);
   }
   cluster_sync_all();
+}
+
+// fp32 workspace (row stride ldw) -> bf16 C (row stride ldc), round to
+// nearest even.  Eight columns per thread; vector loads and stores when the
+// row has eight columns left and both rows are 16-byte aligned there.
+__global__ void __launch_bounds__(256) cast_f32_to_bf16_kernel(const float* __restrict__ W,
+                                                               int ldw,
+                                                               __nv_bfloat16* __restrict__ C,
+                                                               int ldc, int M, int N) {
+  const int groups = (N + 7) / 8;
+  const long long total = (long long)M * groups;
+  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < total;
+       g += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(g / groups);
+    const int col = (int)(g - (long long)row * groups) * 8;
+    const float* w = W + (long long)row * ldw + col;
+    __nv_bfloat16* c = C + (long long)row * ldc + col;
+    if (col + 8 <= N) {
+      const float4 a = *reinterpret_cast<const float4*>(w);
+      const float4 b = *reinterpret_cast<const float4*>(w + 4);
+      uint4 o;
+      o.x = pack_bf16x2(__float_as_uint(a.x), __float_as_uint(a.y));
+      o.y = pack_bf16x2(__float_as_uint(a.z), __float_as_uint(a.w));
+      o.z = pack_bf16x2(__float_as_uint(b.x), __float_as_uint(b.y));
+      o.w = pack_bf16x2(__float_as_uint(b.z), __float_as_uint(b.w));
+      *reinterpret_cast<uint4*>(c) = o;
+    } else {
+      for (int i = 0; col + i < N; ++i) c[i] = __float2bfloat16_rn(w[i]);
+    }
+  }
 }
 
 }  // namespace b200

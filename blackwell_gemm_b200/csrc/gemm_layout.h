@@ -36,6 +36,13 @@ constexpr int kStoreBufBytes = 32 * kStoreCols * 2;        // 4 KiB: 32 rows x 6
 constexpr int kSmemBudget = 227 * 1024;                    // opt-in shared memory per CTA
 constexpr int kSmemReserve = 1024 + 1024;                  // 1 KiB alignment + static/barriers
 
+// Output modes of the epilogue.
+enum OutMode : int {
+  kOutBf16 = 0,    // C bf16 = round(acc)                    (the GEMM)
+  kOutF32 = 1,     // C fp32 = acc                           (K-split partials)
+  kOutF32Add = 2,  // C fp32 += acc, by TMA reduce-add       (split-K workspace)
+};
+
 // Kernel configuration.
 //   kSlabs  K slabs of 64 per pipeline stage (stage K = 64 * kSlabs)
 //   kNSub   256-wide N sub-tiles per pair tile: 1 -> 256 x 256 pair tiles with

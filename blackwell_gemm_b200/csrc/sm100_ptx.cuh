@@ -127,6 +127,16 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, uint32_t src,
                : "memory");
 }
 
+// Element-wise add of a shared-memory tile into global memory (fp32 here):
+// the TMA unit performs the read-modify-write, so concurrent adds from
+// different CTAs into the same tile are safe.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, uint32_t src, int x,
+                                                  int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
+               :: "l"(reinterpret_cast<uint64_t>(m)), "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

@@ -45,7 +45,28 @@ extern "C" {
 int b200_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
                    int ldc, void* stream);
 
-/* Same GEMM with the intra-kernel profiler on.  `profiler` is a device int64
+/* fp32 C = A * B^T without rounding (the per-rank partial of a K-split GEMM:
+ * partials are summed, then rounded once).  C row stride ldc is in floats
+ * (a multiple of 4); other requirements as b200_gemm_bf16.  No reference
+ * counterpart: the reference writes bf16 only. */
+int b200_gemm_bf16_f32out(const void* A, const void* B, float* C, int M, int N, int K, int lda,
+                          int ldb, int ldc, void* stream);
+
+/* bf16 C = round-to-nearest-even(W) for an fp32 M x N matrix W (row stride
+ * ldw floats, a multiple of 4; C row stride ldc, a multiple of 8).  The last
+ * step of a K-split GEMM after the partials are summed.  No reference
+ * counterpart. */
+int b200_cast_f32_bf16(const float* W, int ldw, void* C, int ldc, int M, int N, void* stream);
+
+/* Split-K for grids too small to occupy every SM (skinny M or N): 0 = chosen
+ * per shape (default, B200_GEMM_SPLITS overrides), 1 = never, n = n slices.
+ * Split-K calls accumulate into an fp32 workspace taken from a per-device
+ * stream-ordered pool on the call's stream, then round once to bf16.
+ * b200_gemm_get_splits reports the slice count a call would use. */
+int b200_gemm_set_splits(int splits);
+int b200_gemm_get_splits(int M, int N, int K, int* splits);
+
+/* Same GEMM with the intra-kernel profiler on (never split).  `profiler` is a device int64
  * buffer of rows x (1 + 4 * num_entries) entries, rows from
  * b200_gemm_profile_rows; row r = block * warps_per_cta + warp (warps per
  * CTA = threads from b200_gemm_launch_shape / 32) holds

@@ -1,0 +1,116 @@
+"""Host logic of the multi-GPU configurations on CPU ranks (gloo, 2 processes):
+row sharding and the K-split reduce-scatter, with a plain fp32 GEMM standing
+in for the kernel (the GPU runs use the package's kernels).  Also checks that
+a rank that fails makes its peers' next collective end with an error instead
+of waiting for ever."""
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from blackwell_gemm_b200 import distributed as bdist
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def cpu_gemm_f32(A, Bt):
+    return A.float() @ Bt.float().T
+
+
+def cpu_cast(W):
+    return W.to(torch.bfloat16)
+
+
+def operands(M, N, K, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    Bt = torch.randn(N, K, generator=g).to(torch.bfloat16)
+    return A, Bt
+
+
+def _worker(rank, world, port, case, errq):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        from datetime import timedelta
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=timedelta(seconds=10))
+        M, N, K = 64, 48, 96
+        A, Bt = operands(M, N, K)
+        full = (A.float() @ Bt.float().T)
+        if case == "k_split":
+            ks = bdist.k_slice(K, world, rank)
+            rows = bdist.k_split_gemm(A[:, ks].contiguous(), Bt[:, ks].contiguous(),
+                                      gemm_f32=cpu_gemm_f32, cast=cpu_cast)
+            mine = full[rank * M // world:(rank + 1) * M // world]
+            assert rows.dtype == torch.bfloat16 and rows.shape == mine.shape
+            # summed in fp32 across ranks, rounded once
+            assert torch.allclose(rows.float(), mine.to(torch.bfloat16).float(), rtol=1e-2,
+                                  atol=1e-2)
+            err = (rows.float() - mine).norm() / mine.norm()
+            assert err < 5e-3, float(err)
+        elif case == "row_shard":
+            rs = slice(rank * M // world, (rank + 1) * M // world)
+            rows = bdist.row_shard_gemm(A[rs], Bt, gemm=lambda a, b: cpu_cast(cpu_gemm_f32(a, b)))
+            assert torch.equal(rows, full[rs].to(torch.bfloat16))
+        elif case == "rank_fails":
+            if rank == 1:
+                raise SystemExit(0)          # leaves before the collective
+            ks = bdist.k_slice(K, world, rank)
+            try:
+                bdist.k_split_gemm(A[:, ks].contiguous(), Bt[:, ks].contiguous(),
+                                   gemm_f32=cpu_gemm_f32, cast=cpu_cast)
+            except Exception:
+                errq.put((rank, "timed-out-as-expected"))
+                return
+            raise AssertionError("collective completed although a rank had left")
+        dist.destroy_process_group()
+        errq.put((rank, "ok"))
+    except SystemExit:
+        errq.put((rank, "left"))
+    except Exception:
+        errq.put((rank, traceback.format_exc()))
+
+
+def run(case, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+def test_k_split_reduce_scatter_gloo():
+    out = run("k_split")
+    assert all(v == "ok" for v in out.values()), out
+
+
+def test_row_shard_gloo():
+    out = run("row_shard")
+    assert all(v == "ok" for v in out.values()), out
+
+
+def test_failed_rank_ends_peer_collective_with_error():
+    out = run("rank_fails")
+    assert out[1] == "left"
+    assert out[0] == "timed-out-as-expected", out
+
+
+def test_slicing_rules():
+    assert bdist.k_slice(8, 2, 1) == slice(4, 8)
+    with pytest.raises(ValueError):
+        bdist.k_slice(9, 2, 0)

@@ -290,8 +290,12 @@ def test_profiler_variant_matches_and_records():
     A, Bt = workloads.make_operands(M, N, K, seed=6)
     buf = profiler.alloc(M, N, K, 256)
     C = bg.profile_matmul_b200(A, Bt.T, buf, 256)
-    C0 = bg.matmul_b200(A, Bt.T)
-    torch.cuda.synchronize()
+    capi.set_splits(1)          # the profiled kernel never splits K; compare like with like
+    try:
+        C0 = bg.matmul_b200(A, Bt.T)
+        torch.cuda.synchronize()
+    finally:
+        capi.set_splits(0)
     assert torch.equal(C.view(torch.int16), C0.view(torch.int16))
     warps = profiler.warps_per_cta(M, N, K)
     ev = list(profiler.decode(buf, warps))
