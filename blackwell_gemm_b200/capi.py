@@ -39,6 +39,7 @@ SIGNATURES = {
     "b200_gemm_bf16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "b200_gemm_bf16_profile": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp]),
     "b200_gemm_bf16_f32out": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "b200_gemm_bf16_noalloc": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "b200_cast_f32_bf16": (_i, [_vp, _i, _vp, _i, _i, _i, _vp]),
     "b200_gemm_set_splits": (_i, [_i]),
     "b200_gemm_get_splits": (_i, [_i, _i, _i, _ip]),
@@ -102,6 +103,13 @@ def gemm_bf16_f32out(a_ptr: int, b_ptr: int, c_ptr: int, M: int, N: int, K: int,
 def cast_f32_bf16(w_ptr: int, ldw: int, c_ptr: int, ldc: int, M: int, N: int,
                   stream: int = 0) -> int:
     return lib().b200_cast_f32_bf16(w_ptr, ldw, c_ptr, ldc, M, N, stream)
+
+
+def gemm_bf16_noalloc(a_ptr: int, b_ptr: int, c_ptr: int, M: int, N: int, K: int, lda: int,
+                      ldb: int, ldc: int, stream: int = 0) -> int:
+    """b200_gemm_bf16 without any device allocation (fixed 16 MiB scratch in
+    the library; overlapping calls race).  Returns the status."""
+    return lib().b200_gemm_bf16_noalloc(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, stream)
 
 
 def set_splits(splits: int) -> None:

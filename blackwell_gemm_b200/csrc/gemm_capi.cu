@@ -578,3 +578,140 @@ uint32_t b200_gemm_idesc(int mma_m, int mma_n) { return make_idesc_bf16_f32(mma_
 uint64_t b200_gemm_smem_desc(uint32_t smem_addr) { return make_sdesc_k128(smem_addr); }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot let a library allocate device memory: processes that
+// reserve the GPU's memory up front through their own allocator or arena (a
+// serving engine that sizes its caches to fill HBM leaves nothing for a
+// later cudaMalloc, and a stream-ordered pool growing behind its back breaks
+// its accounting), and latency-critical loops in which cudaMalloc/cudaFree
+// would synchronize the device.  b200_gemm_bf16 allocates on a device's
+// first call (its error word and its split-K pool) and may grow the pool on
+// any split-K call; b200_gemm_bf16_noalloc computes the same GEMM with all
+// of its scratch in the fixed array below, which every GPU that loads this
+// library holds until exit.
+//
+// Layout of the scratch array: bytes [0, 256) hold the kernel's error word
+// (at offset 0), bytes [256, end) the split-K fp32 workspace, so a split-K
+// call fits when M * round_up(N, 8) * 4 <= kNoAllocWorkspaceBytes (16 MiB
+// minus 256 B: e.g. M up to 511 at N = 8192).
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 16u << 20;
+constexpr size_t kNoAllocWorkspaceOffset = 256;
+constexpr size_t kNoAllocWorkspaceBytes = kNoAllocScratchBytes - kNoAllocWorkspaceOffset;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocDevice {
+  bool ready = false;
+  int init_status = B200_OK;
+  DeviceState launch;           // sms and max_pairs only; status/pool stay unset
+  unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
+};
+
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[kMaxDevices];
+
+// Once per device, with that device current: the same architecture checks,
+// shared-memory limits and occupancy query as the allocating path, plus the
+// device address of the scratch array.  None of these calls allocate.
+int noalloc_setup(NoAllocDevice& nd, int dev) {
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return B200_ERR_UNSUPPORTED_DEVICE;
+  if (prop.major != 10 || prop.minor != 0) return B200_ERR_UNSUPPORTED_DEVICE;
+  if (encode_tiled() == nullptr) return B200_ERR_TENSOR_MAP;
+  nd.launch.sms = prop.multiProcessorCount;
+  if (!set_smem_limits<kV256x64>() || !set_smem_limits<kV256x128>() ||
+      !set_smem_limits<kV512x64>() || !set_smem_limit<false, kV256x64, kOutF32Add>())
+    return B200_ERR_LAUNCH;
+  if (query_pairs<kV256x64>(nd.launch.sms, &nd.launch.max_pairs[kV256x64]) != B200_OK ||
+      query_pairs<kV256x128>(nd.launch.sms, &nd.launch.max_pairs[kV256x128]) != B200_OK ||
+      query_pairs<kV512x64>(nd.launch.sms, &nd.launch.max_pairs[kV512x64]) != B200_OK)
+    return B200_ERR_LAUNCH;
+  for (int v = 0; v < kNumVariants; ++v)
+    if (nd.launch.max_pairs[v] < 1) return B200_ERR_LAUNCH;
+  // In host code g_noalloc_scratch names a host-side stand-in; the kernel
+  // must be given the device address.
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+    return B200_ERR_LAUNCH;
+  nd.scratch = static_cast<unsigned char*>(p);
+  return B200_OK;
+}
+
+int noalloc_device(NoAllocDevice** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return B200_ERR_UNSUPPORTED_DEVICE;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return B200_ERR_UNSUPPORTED_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocDevice& nd = g_noalloc_dev[dev];
+  if (!nd.ready) {
+    nd.ready = true;
+    nd.init_status = noalloc_setup(nd, dev);
+    if (nd.init_status != B200_OK) cudaGetLastError();
+  }
+  if (nd.init_status != B200_OK) return nd.init_status;
+  *out = &nd;
+  return B200_OK;
+}
+
+int run_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                     int ldb, int ldc, cudaStream_t stream) {
+  int st = validate(A, B, C, M, N, K, lda, ldb, ldc);
+  if (st != B200_OK) return st;
+  if (M == 0 || N == 0) return B200_OK;
+  NoAllocDevice* nd = nullptr;
+  st = noalloc_device(&nd);
+  if (st != B200_OK) return st;
+  if (K == 0)
+    return cudaMemset2DAsync(C, (size_t)ldc * 2, 0, (size_t)N * 2, M, stream) == cudaSuccess
+               ? B200_OK
+               : B200_ERR_LAUNCH;
+  const long long tiles = ceil_div(M, kPairM) * ceil_div(N, kSubN);
+  const int splits =
+      choose_splits(tiles, (int)ceil_div(K, kSlabK), nd->launch.max_pairs[kV256x64]);
+  const int ldw = (int)ceil_div(N, 8) * 8;
+  const size_t ws_bytes = (size_t)M * ldw * sizeof(float);
+  if (splits > 1 && ws_bytes > kNoAllocWorkspaceBytes) return B200_ERR_TOO_LARGE;
+
+  CUtensorMap ta, tb, tc;
+  if (encode_2d(&ta, A, K, M, lda, kSlabK, kCtaM) != B200_OK ||
+      encode_2d(&tb, B, K, N, ldb, kSlabK, kCtaN) != B200_OK)
+    return B200_ERR_TENSOR_MAP;
+  int* status = reinterpret_cast<int*>(nd->scratch);
+  float* W = reinterpret_cast<float*>(nd->scratch + kNoAllocWorkspaceOffset);
+  // The array keeps the previous call's contents: the error word and the
+  // split-K accumulator must start at zero.
+  if (cudaMemsetAsync(status, 0, sizeof(int), stream) != cudaSuccess) return B200_ERR_LAUNCH;
+  GemmArgs args = base_args(M, N, K, nd->launch, nullptr, 0);
+  args.status = status;
+  if (splits > 1) {
+    if (encode_2d(&tc, W, N, M, ldw, 32, 32, true) != B200_OK) return B200_ERR_TENSOR_MAP;
+    if (cudaMemsetAsync(W, 0, ws_bytes, stream) != cudaSuccess) return B200_ERR_LAUNCH;
+    st = launch<false, kV256x64, kOutF32Add>(ta, tb, tc, args, splits, nd->launch, stream);
+    if (st != B200_OK) return st;
+    return cast_to_bf16(W, ldw, C, ldc, M, N, nd->launch.sms, stream);
+  }
+  if (encode_2d(&tc, C, N, M, ldc, kStoreCols, 32) != B200_OK) return B200_ERR_TENSOR_MAP;
+  switch (choose_variant(M, N, nd->launch.max_pairs)) {
+    case kV256x128:
+      return launch<false, kV256x128, kOutBf16>(ta, tb, tc, args, 1, nd->launch, stream);
+    case kV512x64:
+      return launch<false, kV512x64, kOutBf16>(ta, tb, tc, args, 1, nd->launch, stream);
+    default:
+      return launch<false, kV256x64, kOutBf16>(ta, tb, tc, args, 1, nd->launch, stream);
+  }
+}
+
+}  // namespace
+
+extern "C" int b200_gemm_bf16_noalloc(const void* A, const void* B, void* C, int M, int N,
+                                      int K, int lda, int ldb, int ldc, void* stream) {
+  return run_gemm_noalloc(A, B, C, M, N, K, lda, ldb, ldc, static_cast<cudaStream_t>(stream));
+}

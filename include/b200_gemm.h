@@ -115,6 +115,29 @@ int b200_gemm_wait_probe(unsigned long long timeout_ns, void* stream);
 /* Short text for a status code. */
 const char* b200_gemm_status_string(int status);
 
+/* The same GEMM as b200_gemm_bf16, for callers that cannot let a library
+ * allocate device memory: processes that reserve the GPU's memory up front
+ * through their own allocator or arena (a later cudaMalloc would fail or
+ * break their accounting) and latency-critical loops in which
+ * cudaMalloc/cudaFree would synchronize the device.  b200_gemm_bf16 allocates
+ * on a device's first call (an error word and a split-K memory pool) and its
+ * split-K calls draw workspaces from that pool; this entry point allocates
+ * nothing.  Its scratch is one fixed 16 MiB device array in the library,
+ * held by every GPU that loads the library until exit: a 4-byte error word
+ * plus a split-K fp32 workspace of 16 MiB - 256 B.  A call that would split K
+ * fits when M * round_up(N, 8) * 4 bytes <= 16 MiB - 256 B and otherwise
+ * returns B200_ERR_TOO_LARGE; calls that do not split K use only the error
+ * word, so every shape b200_gemm_bf16 runs without splitting runs here too.
+ * Every call shares the array and clears the parts that must start at zero;
+ * calls whose executions overlap on the GPU (other streams, other threads)
+ * race on it, so callers serialise them.  A pipeline wait that runs out is
+ * recorded only in this array's error word, which no entry point reads.
+ * The first call on a device also sets that device up (kernel attributes,
+ * occupancy, the array's device address); make that first call before any
+ * stream capture.  No counterpart in the reference, which has no scratch. */
+int b200_gemm_bf16_noalloc(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                           int ldb, int ldc, void* stream);
+
 /* Host-side layout rules, exported so they can be checked without a GPU. */
 void b200_gemm_tile_coord(int t, int tiles_m, int tiles_n, int group, int* tm, int* tn);
 uint32_t b200_gemm_idesc(int mma_m, int mma_n);

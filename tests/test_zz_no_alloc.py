@@ -1,0 +1,63 @@
+"""b200_gemm_bf16_noalloc: the GEMM for callers that cannot let a library
+allocate device memory (processes that reserve GPU memory up front through
+their own allocator, loops where a cudaMalloc/cudaFree would synchronize the
+device).  Called through the C ABI and compared with b200_gemm_bf16 on the
+same inputs, on two calls in a row, within the parity tolerance the other
+tests use.  The file name makes pytest collect it last.
+"""
+import pytest
+import torch
+
+from blackwell_gemm_b200 import capi, parity, workloads
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(16, 8192, 8192),      # skinny: split-K through the fixed workspace
+          (1024, 1024, 1024),    # not split: only the error word is used
+          (300, 520, 4096)]      # ragged
+
+
+def run(fn, A, Bt, C):
+    M, K = A.shape
+    N = Bt.shape[0]
+    st = fn(A.data_ptr(), Bt.data_ptr(), C.data_ptr(), M, N, K, K, K, C.stride(0),
+            torch.cuda.current_stream().cuda_stream)
+    assert st == capi.OK, capi.status_string(st)
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_noalloc_matches_allocating_entry_point_twice(M, N, K):
+    capi.set_splits(0)
+    A, Bt = workloads.make_operands(M, N, K, seed=M + N, weight_std=0.02)
+    ldc = (N + 7) // 8 * 8
+    ref = torch.zeros(M, ldc, dtype=torch.bfloat16, device="cuda")
+    run(capi.gemm_bf16, A, Bt, ref)
+    outs = [torch.zeros_like(ref) for _ in range(2)]
+    torch.cuda.synchronize()
+    free_before = None
+    for i, C in enumerate(outs):
+        run(capi.gemm_bf16_noalloc, A, Bt, C)
+        torch.cuda.synchronize()
+        if i == 0:
+            free_before = torch.cuda.mem_get_info()[0]
+    assert torch.cuda.mem_get_info()[0] == free_before     # the second call took no memory
+    for C in outs:
+        m = parity.metrics(C[:, :N], ref[:, :N].float(), A, Bt)
+        assert m["max_scaled"] <= parity.MAX_SCALED_TOL and m["rel_fro"] <= parity.REL_FRO_TOL, m
+        m = parity.metrics(C[:, :N], A.float() @ Bt.float().T, A, Bt)
+        assert parity.passes(m), m
+
+
+def test_noalloc_rejects_workspace_beyond_its_fixed_size():
+    # forcing split-K on a 4096 x 4096 output needs 64 MiB of workspace
+    M = N = 4096
+    A, Bt = workloads.make_operands(M, N, 512, seed=1)
+    C = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    capi.set_splits(4)
+    try:
+        st = capi.gemm_bf16_noalloc(A.data_ptr(), Bt.data_ptr(), C.data_ptr(), M, N, 512, 512,
+                                    512, N, 0)
+    finally:
+        capi.set_splits(0)
+    assert st == capi.ERR_TOO_LARGE
+    assert "exceeds" in capi.status_string(st)
