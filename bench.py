@@ -273,6 +273,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip e2e, baselines and the CPU sample (timing only)")
+    ap.add_argument("--mode", choices=["rows", "ksplit"], default="rows",
+                    help="rows: 8192^3 per GPU, rows of A sharded (default, the headline); "
+                         "ksplit: 8192 x 8192 x 131072 with K split across the GPUs, "
+                         "fp32 partials summed by an NCCL reduce-scatter")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -286,6 +290,8 @@ def main():
 
     if args.impl == "reference":
         return run_reference(args, world, rank, dev)
+    if args.mode == "ksplit":
+        return run_ksplit(args, world, rank, dev)
 
     import torch.distributed as dist
     if world > 1:
@@ -412,6 +418,73 @@ def main():
         }
         line.update(extras)
         print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_ksplit(args, world, rank, dev):
+    """Configuration 5b: C = A B^T with M = N = 8192 and K = 131072 split
+    across the ranks (strong scaling).  One step = this rank's fp32 partial
+    (our kernel, b200_gemm_bf16_f32out) + NCCL reduce-scatter (sum) + bf16
+    cast of this rank's rows, all inside the CUDA events; max over ranks."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    from blackwell_gemm_b200 import distributed as bdist
+    from blackwell_gemm_b200.workloads import K_SPLIT, make_operands
+    M, N, K = K_SPLIT
+    Kr = K // world
+    A, _ = make_operands(M, 8, Kr, seed=2000 + rank, device=dev)
+    _, Bt = make_operands(8, N, Kr, seed=3000 + rank, device=dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    group = dist.group.WORLD if world > 1 else None
+
+    def step():
+        partial = bdist.gemm_f32_cuda(A, Bt)
+        if world > 1:
+            out = torch.empty(M // world, N, dtype=torch.float32, device=dev)
+            dist.reduce_scatter_tensor(out, partial, op=dist.ReduceOp.SUM, group=group)
+        else:
+            out = partial
+        return bdist.cast_bf16_cuda(out)
+
+    step()
+    torch.cuda.synchronize()
+    time.sleep(IDLE_BEFORE_ARM_S)
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    starts, ends = cold_l2_loop(step, args.steps, stream, flush)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    t = torch.tensor([sum(ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t[0])
+    flops = 2 * M * N * K
+    if rank == 0:
+        print(json.dumps({
+            "metric": "BF16 GEMM TFLOP/s (cold-L2), K-split 8192 x 8192 x 131072",
+            "value": flops * args.steps / (total_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "K-split GEMM: per-rank fp32 partial, NCCL reduce-scatter "
+                                   "(sum) over NVLink, bf16 cast",
+                       "M": M, "N": N, "K": K, "k_per_gpu": Kr,
+                       "l2": "flushed: 256 MB written before every step",
+                       "parallelism": f"k-split{world}"},
+            "step_ms": step_stats(ms), "impl": "ours", "gpu_launches": 2 * args.steps,
+            "parity": "tests/test_splitk_gpu.py::test_k_split_and_row_shard_on_two_gpus",
+        }), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
