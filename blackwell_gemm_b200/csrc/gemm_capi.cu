@@ -21,6 +21,7 @@
 
 #include "b200_gemm.h"
 #include "gemm_kernel.cuh"
+#include "gemm_skinny.cuh"
 
 using namespace b200;
 
@@ -63,6 +64,7 @@ struct DeviceState {
   int max_pairs[kNumVariants] = {0, 0, 0};  // co-resident 2-CTA clusters per variant
   int* status = nullptr;                    // device error word
   cudaMemPool_t pool = nullptr;             // stream-ordered split-K workspaces
+  int sk_clusters[16][4] = {};              // skinny-cluster kernels: resident clusters of 1,2,4,8
 };
 
 std::mutex g_mu;
@@ -159,6 +161,72 @@ bool set_smem_limits() {
   return set_smem_limit<false, V, kOutBf16>() && set_smem_limit<true, V, kOutBf16>();
 }
 
+template <int kMp, int kSlabs>
+bool set_skinny_limit() {
+  return cudaFuncSetAttribute(gemm_skinny_kernel<kMp, kSlabs>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              SkinnyCfg<kMp, kSlabs>::kSmemBytes) == cudaSuccess;
+}
+
+template <int kSlabs>
+bool set_skinny_limits_for() {
+  return set_skinny_limit<16, skinny_fit_slabs(16, kSlabs)>() &&
+         set_skinny_limit<32, skinny_fit_slabs(32, kSlabs)>() &&
+         set_skinny_limit<64, skinny_fit_slabs(64, kSlabs)>() &&
+         set_skinny_limit<128, skinny_fit_slabs(128, kSlabs)>() &&
+         set_skinny_limit<256, skinny_fit_slabs(256, kSlabs)>();
+}
+
+bool set_skinny_limits() {
+  return set_skinny_limits_for<1>() && set_skinny_limits_for<2>() && set_skinny_limits_for<4>();
+}
+
+// Skinny cluster kernels: (Mp, ring depth) per slot of DeviceState::sk_clusters.
+// Shallow rings let two CTAs share an SM, deep ones keep one CTA per SM.
+constexpr int kSkc[][2] = {{16, 5}, {16, 10}, {32, 3}, {32, 9}, {64, 3}, {64, 8}, {128, 6},
+                           {256, 4}};
+constexpr int kNumSkc = 8;
+
+template <int I>
+struct Skc {
+  static constexpr int kMp = kSkc[I][0], kStages = kSkc[I][1];
+  using P = SkinnyClusterCfg<kMp, kStages>;
+  static constexpr auto kernel = gemm_skinny_cluster_kernel<kMp, kStages>;
+};
+
+template <int I>
+bool skc_init(DeviceState& d) {
+  using S = Skc<I>;
+  if (cudaFuncSetAttribute(S::kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           S::P::kSmemBytes) != cudaSuccess)
+    return false;
+  for (int ci = 0; ci < 4; ++ci) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(8 * d.sms, 1, 1);
+    cfg.blockDim = dim3(S::P::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = S::P::kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1u << ci;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, S::kernel, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    d.sk_clusters[I][ci] = n;
+  }
+  return true;
+}
+
+bool skc_init_all(DeviceState& d) {
+  return skc_init<0>(d) && skc_init<1>(d) && skc_init<2>(d) && skc_init<3>(d) &&
+         skc_init<4>(d) && skc_init<5>(d) && skc_init<6>(d) && skc_init<7>(d);
+}
+
 int init_device(DeviceState& d, int dev) {
   cudaDeviceProp prop;
   if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return B200_ERR_UNSUPPORTED_DEVICE;
@@ -167,7 +235,7 @@ int init_device(DeviceState& d, int dev) {
   d.sms = prop.multiProcessorCount;
   if (!set_smem_limits<kV256x64>() || !set_smem_limits<kV256x128>() ||
       !set_smem_limits<kV512x64>() || !set_smem_limit<false, kV256x64, kOutF32>() ||
-      !set_smem_limit<false, kV256x64, kOutF32Add>())
+      !set_smem_limit<false, kV256x64, kOutF32Add>() || !set_skinny_limits())
     return B200_ERR_LAUNCH;
   if (query_pairs<kV256x64>(d.sms, &d.max_pairs[kV256x64]) != B200_OK ||
       query_pairs<kV256x128>(d.sms, &d.max_pairs[kV256x128]) != B200_OK ||
@@ -175,6 +243,7 @@ int init_device(DeviceState& d, int dev) {
     return B200_ERR_LAUNCH;
   for (int v = 0; v < kNumVariants; ++v)
     if (d.max_pairs[v] < 1) return B200_ERR_LAUNCH;
+  if (!skc_init_all(d)) return B200_ERR_LAUNCH;
   if (cudaMalloc(&d.status, sizeof(int)) != cudaSuccess ||
       cudaMemset(d.status, 0, sizeof(int)) != cudaSuccess)
     return B200_ERR_LAUNCH;
@@ -255,7 +324,7 @@ CUtensorMapL2promotion l2_promotion() {
 
 int encode_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
               uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
-              bool fp32 = false) {
+              bool fp32 = false, bool swizzle = true) {
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {row_stride_elems * (fp32 ? 4 : 2)};
   const cuuint32_t box[2] = {box_inner, box_outer};
@@ -263,7 +332,8 @@ int encode_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer
   const CUresult r = encode_tiled()(
       map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
       const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-      CU_TENSOR_MAP_SWIZZLE_128B, l2_promotion(), CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, l2_promotion(),
+      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TENSOR_MAP;
 }
 
@@ -325,6 +395,192 @@ int cast_to_bf16(const float* W, int ldw, void* C, int ldc, int M, int N, int sm
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
 }
 
+// Skinny-M path (M <= 256): C^T = B A^T with B streamed by every SM (see
+// gemm_skinny.cuh).  K is cut so the (128-row block, K slice) units fill
+// the SMs in whole waves: the fewest slices reaching 95 % wave efficiency,
+// else the most efficient, with at least 2 K-blocks per slice.
+int choose_skinny_splits(long long tiles, int k_blocks, int ctas) {
+  const int forced = tuning_splits();
+  if (forced > 0) return forced < k_blocks ? forced : k_blocks;
+  int best = 1;
+  double best_eff = wave_efficiency(tiles, ctas);
+  if (best_eff >= 0.95) return 1;
+  const int max_s = k_blocks / 2 < 64 ? k_blocks / 2 : 64;
+  for (int s2 = 2; s2 <= max_s; ++s2) {
+    const double e = wave_efficiency(tiles * s2, ctas);
+    if (e >= 0.95) return s2;
+    if (e > best_eff + 1e-9) {
+      best_eff = e;
+      best = s2;
+    }
+  }
+  return best;
+}
+
+constexpr int kSkinnyMaxM = 256;
+
+template <int kMp, int kSlabs>
+int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
+                  int ldc, DeviceState& d, cudaStream_t stream) {
+  using P = SkinnyCfg<kMp, kSlabs>;
+  CUtensorMap tb, ta, tw;
+  if (encode_2d(&tb, B, K, N, ldb, kSlabK, P::kRowsB) != B200_OK ||
+      encode_2d(&ta, A, K, M, lda, kSlabK, kMp) != B200_OK)
+    return B200_ERR_TENSOR_MAP;
+  SkinnyArgs args;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.tiles = (int)ceil_div(N, P::kRowsB);
+  args.k_blocks = (int)ceil_div(K, P::kBK);
+  int splits = choose_skinny_splits(args.tiles, args.k_blocks, d.sms);
+  args.kb_per_split = (int)ceil_div(args.k_blocks, splits);
+  args.splits = (int)ceil_div(args.k_blocks, args.kb_per_split);
+  args.status = d.status;
+  args.timeout_ns = g_timeout_ns.load();
+  const int ldw = (int)ceil_div(N, 8) * 8;
+  const size_t bytes = (size_t)M * ldw * sizeof(float);
+  float* W = nullptr;
+  if (cudaMallocFromPoolAsync(reinterpret_cast<void**>(&W), bytes, d.pool, stream) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return B200_ERR_LAUNCH;
+  }
+  int st = encode_2d(&tw, W, N, M, ldw, 32, P::kChunk, true, false);
+  if (st == B200_OK && cudaMemsetAsync(W, 0, bytes, stream) != cudaSuccess) st = B200_ERR_LAUNCH;
+  if (st == B200_OK) {
+    const long long units = (long long)args.tiles * args.splits;
+    const int grid = (int)(units < d.sms ? units : d.sms);
+    gemm_skinny_kernel<kMp, kSlabs><<<grid, P::kThreads, P::kSmemBytes, stream>>>(tb, ta, tw,
+                                                                                args);
+    if (cudaGetLastError() != cudaSuccess) st = B200_ERR_LAUNCH;
+  }
+  if (st == B200_OK) st = cast_to_bf16(W, ldw, C, ldc, M, N, d.sms, stream);
+  cudaFreeAsync(W, stream);
+  return st;
+}
+
+template <int kSlabs>
+int run_skinny_slabs(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
+                     int ldc, DeviceState& d, cudaStream_t stream) {
+  if (M <= 16)
+    return launch_skinny<16, skinny_fit_slabs(16, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
+                                                            stream);
+  if (M <= 32)
+    return launch_skinny<32, skinny_fit_slabs(32, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
+                                                            stream);
+  if (M <= 64)
+    return launch_skinny<64, skinny_fit_slabs(64, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
+                                                            stream);
+  if (M <= 128)
+    return launch_skinny<128, skinny_fit_slabs(128, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
+                                                              stream);
+  return launch_skinny<256, skinny_fit_slabs(256, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
+                                                            stream);
+}
+
+// K slabs per stage of the skinny kernel (B200_GEMM_SKINNY_SLABS: 1, 2, 4).
+int skinny_slabs() {
+  static const int s = env_int("B200_GEMM_SKINNY_SLABS", 2, 1, 4);
+  return s;
+}
+
+// Cluster split-K: the largest cluster (8, 4, 2, 1) whose grid of
+// tiles x S CTAs fits in one wave, keeping >= 8 K-blocks per rank.
+template <int I>
+int launch_skinny_cluster(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                          int ldb, int ldc, DeviceState& d, cudaStream_t stream) {
+  using S = Skc<I>;
+  const long long tiles = ceil_div(N, S::P::kRowsB);
+  const int k_blocks = (int)ceil_div(K, kSlabK);
+  int ci = 0;
+  const int forced = tuning_splits();
+  if (forced > 0) {
+    while (ci < 3 && (2 << ci) <= forced) ++ci;
+  } else {
+    for (int c = 3; c >= 1; --c) {
+      const long long clusters = d.sk_clusters[I][c];
+      if (clusters > 0 && tiles <= clusters && k_blocks >= 8 * (1 << c)) {
+        ci = c;
+        break;
+      }
+    }
+  }
+  if (d.sk_clusters[I][ci] < 1) return B200_ERR_LAUNCH;
+  const int csize = 1 << ci;
+  CUtensorMap tb, ta;
+  if (encode_2d(&tb, B, K, N, ldb, kSlabK, S::P::kRowsB) != B200_OK ||
+      encode_2d(&ta, A, K, M, lda, kSlabK, S::kMp) != B200_OK)
+    return B200_ERR_TENSOR_MAP;
+  SkinnyClusterArgs args;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.k_blocks = k_blocks;
+  args.kb_per = (int)ceil_div(k_blocks, csize);
+  args.ldc = ldc;
+  args.C = static_cast<__nv_bfloat16*>(C);
+  args.status = d.status;
+  args.timeout_ns = g_timeout_ns.load();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(tiles * csize), 1, 1);
+  cfg.blockDim = dim3(S::P::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = S::P::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, S::kernel, tb, ta, args) != cudaSuccess) {
+    cudaGetLastError();
+    return B200_ERR_LAUNCH;
+  }
+  return B200_OK;
+}
+
+// Ring-depth preference of the cluster kernels: 1 = one deep ring per SM
+// (default, measured faster), 2 = two CTAs per SM where the M bucket allows.
+int skinny_occupancy() {
+  static const int o = env_int("B200_GEMM_SKINNY_OCC", 1, 1, 2);
+  return o;
+}
+
+int run_skinny_cluster(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                       int ldb, int ldc, DeviceState& d, cudaStream_t stream) {
+  const bool two = skinny_occupancy() == 2;
+#define B200_SKC(I) launch_skinny_cluster<I>(A, B, C, M, N, K, lda, ldb, ldc, d, stream)
+  if (M <= 16) return two ? B200_SKC(0) : B200_SKC(1);
+  if (M <= 32) return two ? B200_SKC(2) : B200_SKC(3);
+  if (M <= 64) return two ? B200_SKC(4) : B200_SKC(5);
+  if (M <= 128) return B200_SKC(6);
+  return B200_SKC(7);
+#undef B200_SKC
+}
+
+int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
+               int ldc, DeviceState& d, cudaStream_t stream) {
+  // Up to 16 rows of A the single-launch cluster kernel is faster (no
+  // workspace clear or rounding pass); above, the persistent kernel streams
+  // better.  B200_GEMM_SKINNY=2 forces the cluster kernel for every M.
+  static const int mode = env_int("B200_GEMM_SKINNY", 1, 0, 2);
+  if (mode == 2 || M <= 16) return run_skinny_cluster(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
+  switch (skinny_slabs()) {
+    case 1: return run_skinny_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
+    case 4: return run_skinny_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
+    default: return run_skinny_slabs<2>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
+  }
+}
+
+// Skinny path for M <= 256 when B is large enough to need every SM and K
+// deep enough to be worth streaming (B200_GEMM_SKINNY=0 disables it).
+bool use_skinny(int M, int N, int K) {
+  static const int enabled = env_int("B200_GEMM_SKINNY", 1, 0, 2);
+  return enabled && M <= kSkinnyMaxM && N >= 1024 && K >= 512;
+}
+
 GemmArgs base_args(int M, int N, int K, const DeviceState& d, long long* prof, int entries) {
   GemmArgs args;
   args.M = M;
@@ -365,6 +621,8 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda
       encode_2d(&tc, C, N, M, ldc, kStoreCols, 32) != B200_OK)
     return B200_ERR_TENSOR_MAP;
 
+  if (!kProfile && use_skinny(M, N, K))
+    return run_skinny(A, B, C, M, N, K, lda, ldb, ldc, *d, stream);
   GemmArgs args = base_args(M, N, K, *d, prof, prof_entries);
   // Split-K (not with the profiler): tiles accumulate their K slices into a
   // zeroed fp32 workspace by TMA reduce-add, then one pass rounds to bf16.

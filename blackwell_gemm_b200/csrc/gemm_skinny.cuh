@@ -1,0 +1,439 @@
+// Skinny-M GEMM for sm_100a (M <= 256, the HBM-bound decode shapes):
+// C = A * B^T computed as C^T = B * A^T, so the big operand B supplies the
+// MMA's 128-row M dimension and the few rows of A its N dimension
+// (Mp = M rounded up to a supported MMA N of 16..256).  The tensor core then
+// does almost no wasted work and each SM only streams its share of B
+// through a deep shared-memory ring; the reference can run none of these
+// shapes except v1 at M = 128 (its kernels need M % 256 == 0).
+//
+// One CTA per SM, persistent over work units (128-row block of B, K slice);
+// cta_group::1 tcgen05.mma M=128 N=Mp K=16 into a double-buffered TMEM
+// accumulator (128 lanes x Mp fp32 columns per buffer).  Warp roles:
+//   warp 0     TMA producer (B box 64 x 128, A box 64 x Mp)
+//   warp 1     TMEM owner and MMA issuer
+//   warps 2-5  epilogue: TMEM lane quarter -> smem [m][n] fp32 -> TMA
+//              reduce-add into the zeroed fp32 workspace W (M x N); a
+//              separate pass rounds W to bf16 C.  (Finishing a tile inside
+//              the kernel, by the warp whose reduce-adds complete last, was
+//              measured slower: waiting for each unit's reduce-adds stalls
+//              the epilogue, which stalls the MMA.)
+// All waits are the bounded waits of gemm_kernel.cuh.
+#pragma once
+#include "gemm_kernel.cuh"
+
+namespace b200 {
+
+template <int kMp, int kSlabs>
+struct SkinnyCfg {
+  static_assert(kMp % 16 == 0 && kMp >= 16 && kMp <= 256, "MMA N must be 16..256, step 16");
+  static constexpr int kRowsB = 128;                       // MMA M: rows of B per unit
+  static constexpr int kBK = kSlabs * kSlabK;              // K per stage
+  static constexpr int kSlabB = kRowsB * kSlabK * 2;       // 16 KiB
+  static constexpr int kSlabA = kMp * kSlabK * 2;
+  static constexpr int kBytesB = kSlabs * kSlabB;
+  static constexpr int kBytesA = kSlabs * kSlabA;
+  static constexpr int kStageBytes = kBytesB + kBytesA;
+  static constexpr int kChunk = kMp < 32 ? kMp : 32;       // epilogue columns per pass
+  static constexpr int kStoreBuf = 32 * kChunk * 4;        // [kChunk m][32 n] fp32
+  static constexpr int kStoreBytes = 4 * 2 * kStoreBuf;    // 4 warps x 2 buffers
+  static constexpr int kStagesFit = (kSmemBudget - kStoreBytes - kSmemReserve) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 16 ? 16 : kStagesFit;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kStoreBytes + 1024;
+  static constexpr int kTmemAlloc = 2 * kMp <= 32 ? 32 : 2 * kMp;  // power of two >= 32
+  static constexpr int kThreads = 192;
+  static_assert(kStages >= 2, "ring too shallow");
+};
+
+// Largest K-slab count <= `want` whose stages still leave a ring of three.
+constexpr int skinny_fit_slabs(int mp, int want) {
+  for (int s = want; s > 1; --s) {
+    const int chunk = mp < 32 ? mp : 32;
+    const int store = 4 * 2 * 32 * chunk * 4;
+    const int stage = s * (128 * kSlabK * 2 + mp * kSlabK * 2);
+    if ((kSmemBudget - store - kSmemReserve) / stage >= 3) return s;
+  }
+  return 1;
+}
+
+struct SkinnyArgs {
+  int M, N, K;
+  int tiles;         // ceil(N / 128)
+  int k_blocks;      // ceil(K / kBK)
+  int splits;        // K slices per tile
+  int kb_per_split;
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+template <int kMp, int kSlabs>
+__global__ void __launch_bounds__(192, 1)
+gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 64 x 128
+                   const __grid_constant__ CUtensorMap tmap_a,   // M x K, box 64 x Mp
+                   const __grid_constant__ CUtensorMap tmap_w,   // W fp32 M x N, box 32 x kChunk
+                   const SkinnyArgs args) {
+  using P = SkinnyCfg<kMp, kSlabs>;
+  constexpr int kStages = P::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ alignas(8) uint64_t bar_full[kStages];
+  __shared__ alignas(8) uint64_t bar_empty[kStages];
+  __shared__ alignas(8) uint64_t bar_acc_full[2];
+  __shared__ alignas(8) uint64_t bar_acc_empty[2];
+  __shared__ alignas(8) uint64_t bar_drain;
+  __shared__ uint32_t tmem_slot;
+  __shared__ uint32_t abort_word;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int units = args.tiles * args.splits;
+  const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t store_base = smem_base + kStages * P::kStageBytes;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&bar_full[s]), 1);
+      mbar_init(smem_u32(&bar_empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&bar_acc_full[b]), 1);
+      mbar_init(smem_u32(&bar_acc_empty[b]), 4);
+    }
+    mbar_init(smem_u32(&bar_drain), 1);
+    abort_word = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc_1(smem_u32(&tmem_slot), P::kTmemAlloc);
+    tmem_relinquish_1();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = tmem_slot;
+
+  WaitCtx wctx;
+  wctx.status = args.status;
+  wctx.timeout_ns = args.timeout_ns;
+  wctx.abort_local = smem_u32(&abort_word);
+  wctx.abort_peer = smem_u32(&abort_word);  // no peer CTA: both words are this CTA's
+
+  auto unit_range = [&](int u, int* tile, int* kb0, int* kb1) {
+    *tile = u / args.splits;
+    const int s = u - *tile * args.splits;
+    *kb0 = s * args.kb_per_split;
+    const int end = *kb0 + args.kb_per_split;
+    *kb1 = end < args.k_blocks ? end : args.k_blocks;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        int tile, kb0, kb1;
+        unit_range(u, &tile, &kb0, &kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!wait_bounded(smem_u32(&bar_empty[stage]), phase ^ 1u, wctx, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sb = smem_base + stage * P::kStageBytes;
+          const uint32_t fb = smem_u32(&bar_full[stage]);
+          mbar_arrive_expect_tx(fb, P::kStageBytes);
+          // B's slabs first, back to back, so each row's consecutive 128 B
+          // segments are requested together.
+#pragma unroll
+          for (int sl = 0; sl < kSlabs; ++sl)
+            tma_load_2d(sb + sl * P::kSlabB, &tmap_b, kb * P::kBK + sl * kSlabK,
+                        tile * P::kRowsB, fb);
+#pragma unroll
+          for (int sl = 0; sl < kSlabs; ++sl)
+            tma_load_2d(sb + P::kBytesB + sl * P::kSlabA, &tmap_a, kb * P::kBK + sl * kSlabK, 0,
+                        fb);
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_bf16_f32(P::kRowsB, kMp);
+      uint32_t stage = 0, phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++it) {
+        int tile, kb0, kb1;
+        unit_range(u, &tile, &kb0, &kb1);
+        const uint32_t buf = it & 1, acc_phase = (it >> 1) & 1;
+        if (!wait_bounded(smem_u32(&bar_acc_empty[buf]), acc_phase ^ 1u, wctx, kErrWaitAccEmpty))
+          break;
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + buf * kMp;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!wait_bounded(smem_u32(&bar_full[stage]), phase, wctx, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t sb = smem_base + stage * P::kStageBytes;
+#pragma unroll
+          for (int sl = 0; sl < kSlabs; ++sl) {
+            const uint64_t bdesc_big = make_sdesc_k128(sb + sl * P::kSlabB);
+            const uint64_t adesc_small = make_sdesc_k128(sb + P::kBytesB + sl * P::kSlabA);
+#pragma unroll
+            for (int k = 0; k < kSlabK / kMmaK; ++k)
+              umma_bf16_1(d_tmem, bdesc_big + 2ull * k, adesc_small + 2ull * k, idesc,
+                          (kb != kb0 || sl != 0 || k != 0) ? 1u : 0u);
+          }
+          umma_commit_1(smem_u32(&bar_empty[stage]));
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_1(smem_u32(&bar_acc_full[buf]));
+      }
+      umma_commit_1(smem_u32(&bar_drain));
+      if (!mbar_try_wait(smem_u32(&bar_drain), 0))
+        wait_slow(smem_u32(&bar_drain), 0, wctx, kErrWaitDrain, false);
+    }
+    __syncwarp();
+  } else {
+    // Epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = rows n of B.
+    const int quarter = warp & 3;
+    const uint32_t my_store = store_base + (warp - 2) * 2 * P::kStoreBuf;
+    uint32_t nstore = 0;
+    int it = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+      int tile, kb0, kb1;
+      unit_range(u, &tile, &kb0, &kb1);
+      const uint32_t buf = it & 1, acc_phase = (it >> 1) & 1;
+      int ok = 0;
+      if (lane == 0) ok = wait_bounded(smem_u32(&bar_acc_full[buf]), acc_phase, wctx, kErrWaitAccFull);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after_sync();
+      const uint32_t tbase = tmem_base + buf * kMp + ((uint32_t)(quarter * 32) << 16);
+      const int n0 = tile * P::kRowsB + quarter * 32;
+#pragma unroll 1
+      for (int c = 0; c < kMp / P::kChunk; ++c) {
+        uint32_t v[P::kChunk];
+        if constexpr (P::kChunk == 16) {
+          tmem_ld_32x32b_x16(tbase + c * 16, *reinterpret_cast<uint32_t(*)[16]>(v));
+        } else {
+          tmem_ld_32x32b_x32(tbase + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v));
+        }
+        tmem_wait_ld();
+        if (c == kMp / P::kChunk - 1) {
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_local(smem_u32(&bar_acc_empty[buf]));
+        }
+        const uint32_t sb = my_store + (nstore & 1u) * P::kStoreBuf;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        // Row j of the box is m = c*kChunk + j; column `lane` is n = n0 + lane.
+#pragma unroll
+        for (int j = 0; j < P::kChunk; ++j) st_shared_u32(sb + j * 128u + lane * 4u, v[j]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&tmap_w, sb, n0, c * P::kChunk);
+          bulk_commit_group();
+        }
+        ++nstore;
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc_1(tmem_base, P::kTmemAlloc);
+  }
+}
+
+}  // namespace b200
+
+namespace b200 {
+
+// ---------------------------------------------------------------------------
+// Cluster split-K variant: no workspace, one launch.  A cluster of S CTAs
+// (S = 1, 2, 4 or 8, a launch attribute) owns one 128-row block of B; CTA r
+// of the cluster accumulates K blocks [r * kb_per, (r+1) * kb_per) into its
+// own TMEM.  The S partial sums are then added through distributed shared
+// memory 32 output columns (= rows of C) at a time: every CTA copies its
+// TMEM chunk c into a shared staging slot, the cluster synchronises, CTA
+// (c % S) adds the S slots and writes bf16 C, the cluster synchronises again
+// before the slot is reused.  The grid is not persistent: blocks x S CTAs,
+// one work unit each.
+template <int kMp, int kStagesWanted>
+struct SkinnyClusterCfg {
+  static constexpr int kRowsB = 128;
+  static constexpr int kSlabB = kRowsB * kSlabK * 2;      // 16 KiB
+  static constexpr int kSlabA = kMp * kSlabK * 2;
+  static constexpr int kStageBytes = kSlabB + kSlabA;
+  static constexpr int kChunk = kMp < 32 ? kMp : 32;      // rows of C reduced per pass
+  static constexpr int kSlotBytes = kChunk * kRowsB * 4;  // [kChunk m][128 n] fp32
+  static constexpr int kStages = kStagesWanted;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 2 * kSlotBytes + 1024;
+  static constexpr int kTmemAlloc = kMp <= 32 ? 32 : kMp;
+  static constexpr int kThreads = 192;
+  static_assert(kSmemBytes <= kSmemBudget - 1024, "does not fit in shared memory");
+};
+
+struct SkinnyClusterArgs {
+  int M, N, K;
+  int k_blocks;       // ceil(K / 64)
+  int kb_per;         // K blocks per cluster rank
+  int ldc;            // C row stride (elements)
+  __nv_bfloat16* C;
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+template <int kMp, int kStages>
+__global__ void __launch_bounds__(192)
+gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 64 x 128
+                           const __grid_constant__ CUtensorMap tmap_a,   // M x K, box 64 x Mp
+                           const SkinnyClusterArgs args) {
+  using P = SkinnyClusterCfg<kMp, kStages>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ alignas(8) uint64_t bar_full[kStages];
+  __shared__ alignas(8) uint64_t bar_empty[kStages];
+  __shared__ alignas(8) uint64_t bar_acc_full;
+  __shared__ uint32_t tmem_slot;
+  __shared__ uint32_t abort_word;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t csize = cluster_nctarank();
+  const int tile = blockIdx.x / (int)csize;
+  const int kb0 = (int)rank * args.kb_per;
+  const int kb1 = kb0 + args.kb_per < args.k_blocks ? kb0 + args.kb_per : args.k_blocks;
+  const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t slot_base = smem_base + kStages * P::kStageBytes;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&bar_full[s]), 1);
+      mbar_init(smem_u32(&bar_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&bar_acc_full), 1);
+    abort_word = 0;
+    fence_mbar_init_cluster();
+    prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_a);
+  }
+  if (warp == 1) {
+    tmem_alloc_1(smem_u32(&tmem_slot), P::kTmemAlloc);
+    tmem_relinquish_1();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = tmem_slot;
+
+  WaitCtx wctx;
+  wctx.status = args.status;
+  wctx.timeout_ns = args.timeout_ns;
+  wctx.abort_local = smem_u32(&abort_word);
+  wctx.abort_peer = smem_u32(&abort_word);
+
+  bool acc_ok = true;
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!wait_bounded(smem_u32(&bar_empty[stage]), phase ^ 1u, wctx, kErrWaitEmpty)) break;
+        const uint32_t sb = smem_base + stage * P::kStageBytes;
+        const uint32_t fb = smem_u32(&bar_full[stage]);
+        mbar_arrive_expect_tx(fb, P::kStageBytes);
+        tma_load_2d(sb, &tmap_b, kb * kSlabK, tile * P::kRowsB, fb);
+        tma_load_2d(sb + P::kSlabB, &tmap_a, kb * kSlabK, 0, fb);
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_bf16_f32(P::kRowsB, kMp);
+      uint32_t stage = 0, phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!wait_bounded(smem_u32(&bar_full[stage]), phase, wctx, kErrWaitFull)) break;
+        tc_fence_after_sync();
+        const uint32_t sb = smem_base + stage * P::kStageBytes;
+        const uint64_t bdesc_big = make_sdesc_k128(sb);
+        const uint64_t adesc_small = make_sdesc_k128(sb + P::kSlabB);
+#pragma unroll
+        for (int k = 0; k < kSlabK / kMmaK; ++k)
+          umma_bf16_1(tmem_base, bdesc_big + 2ull * k, adesc_small + 2ull * k, idesc,
+                      (kb != kb0 || k != 0) ? 1u : 0u);
+        umma_commit_1(smem_u32(&bar_empty[stage]));
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      }
+      // Completes once every MMA above has (also when there were none).
+      umma_commit_1(smem_u32(&bar_acc_full));
+    }
+    __syncwarp();
+  } else {
+    int ok = 0;
+    if (lane == 0) ok = wait_bounded(smem_u32(&bar_acc_full), 0, wctx, kErrWaitAccFull);
+    acc_ok = __shfl_sync(0xffffffffu, ok, 0) != 0;
+    tc_fence_after_sync();
+  }
+
+  // Cluster reduction, 32 (or Mp) rows of C per pass; all 6 warps take part
+  // in the cluster barriers, the 4 epilogue warps move the data.
+  const bool empty_slice = kb1 <= kb0;  // this rank saw no K blocks: its TMEM holds nothing
+  const int quarter = warp & 3;
+  const int n_local = quarter * 32 + lane;       // row of B within the tile = column of C
+  const int n = tile * P::kRowsB + n_local;
+  for (int c = 0; c < kMp / P::kChunk; ++c) {
+    const uint32_t slot = slot_base + (c & 1) * P::kSlotBytes;
+    if (warp >= 2) {
+      uint32_t v[P::kChunk];
+      if (acc_ok && !empty_slice) {
+        if constexpr (P::kChunk == 16)
+          tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quarter * 32) << 16) + c * 16,
+                             *reinterpret_cast<uint32_t(*)[16]>(v));
+        else
+          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + c * 32,
+                             *reinterpret_cast<uint32_t(*)[32]>(v));
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int j = 0; j < P::kChunk; ++j) v[j] = 0u;
+      }
+      // slot[m][n_local]: consecutive lanes write consecutive words
+#pragma unroll
+      for (int j = 0; j < P::kChunk; ++j) st_shared_u32(slot + (j * P::kRowsB + n_local) * 4u, v[j]);
+    }
+    cluster_sync_all();
+    if (warp >= 2 && (c % (int)csize) == (int)rank && n < args.N) {
+      const int m0 = c * P::kChunk;
+#pragma unroll 4
+      for (int j = 0; j < P::kChunk; ++j) {
+        if (m0 + j >= args.M) break;
+        const uint32_t off = slot + (j * P::kRowsB + n_local) * 4u;
+        float acc = 0.f;
+        for (uint32_t r = 0; r < csize; ++r) acc += ld_shared_cluster_f32(cluster_map(off, r));
+        args.C[(long long)(m0 + j) * args.ldc + n] = __float2bfloat16_rn(acc);
+      }
+    }
+    cluster_sync_all();
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc_1(tmem_base, P::kTmemAlloc);
+  }
+}
+
+}  // namespace b200

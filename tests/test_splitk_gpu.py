@@ -178,3 +178,22 @@ def test_k_split_and_row_shard_on_two_gpus():
     for p in ps:
         p.join(timeout=60)
     assert all(ok for _, ok, _ in res), res
+
+
+# ------------------------------------------------------- skinny-M kernel
+@pytest.mark.parametrize("M", [1, 16, 17, 32, 50, 64, 100, 128, 200, 256])
+@pytest.mark.parametrize("N,K", [(1024, 512), (1032, 520), (8200, 1000)])
+def test_skinny_kernel_exact_bits(M, N, K):
+    # M <= 256, N >= 1024, K >= 512 take the C^T = B A^T kernel
+    A, Bt = oracle.exact_inputs(M, N, K, seed=M)
+    C = bf16_gemm(dev(A), dev(Bt))
+    assert np.array_equal(bits(C), oracle.gemm_bf16(A, Bt))
+
+
+@pytest.mark.parametrize("splits", [1, 5, 64])
+def test_skinny_kernel_forced_splits_random(splits):
+    capi.set_splits(splits)
+    M, N, K = 48, 4096, 8192
+    A, Bt = workloads.make_operands(M, N, K, seed=splits, weight_std=0.02)
+    C = bf16_gemm(A, Bt)
+    assert parity.passes(parity.metrics(C, A.float() @ Bt.float().T, A, Bt))
