@@ -396,21 +396,22 @@ int cast_to_bf16(const float* W, int ldw, void* C, int ldc, int M, int N, int sm
 }
 
 // Skinny-M path (M <= 256): C^T = B A^T with B streamed by every SM (see
-// gemm_skinny.cuh).  K is cut so the (128-row block, K slice) units fill
-// the SMs in whole waves: the fewest slices reaching 95 % wave efficiency,
-// else the most efficient, with at least 2 K-blocks per slice.
-int choose_skinny_splits(long long tiles, int k_blocks, int ctas) {
+// gemm_skinny.cuh).  K is cut into slices so the (128-row block, K slice)
+// units fill the SMs, but every slice adds M x N fp32 of reduce-add traffic:
+// the slice count minimises (B bytes + slices x workspace bytes) / wave
+// efficiency, with at least 2 K-blocks per slice (at N = K = 8192: 9 slices
+// up to M = 64, 2 above).
+int choose_skinny_splits(long long tiles, int k_blocks, int ctas, int M, int N, int K) {
   const int forced = tuning_splits();
   if (forced > 0) return forced < k_blocks ? forced : k_blocks;
+  const double b_bytes = 2.0 * N * K, w_bytes = 4.0 * M * N;
   int best = 1;
-  double best_eff = wave_efficiency(tiles, ctas);
-  if (best_eff >= 0.95) return 1;
+  double best_cost = b_bytes / wave_efficiency(tiles, ctas);
   const int max_s = k_blocks / 2 < 64 ? k_blocks / 2 : 64;
   for (int s2 = 2; s2 <= max_s; ++s2) {
-    const double e = wave_efficiency(tiles * s2, ctas);
-    if (e >= 0.95) return s2;
-    if (e > best_eff + 1e-9) {
-      best_eff = e;
+    const double cost = (b_bytes + s2 * w_bytes) / wave_efficiency(tiles * s2, ctas);
+    if (cost < best_cost) {
+      best_cost = cost;
       best = s2;
     }
   }
@@ -433,7 +434,7 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
   args.K = K;
   args.tiles = (int)ceil_div(N, P::kRowsB);
   args.k_blocks = (int)ceil_div(K, P::kBK);
-  int splits = choose_skinny_splits(args.tiles, args.k_blocks, d.sms);
+  int splits = choose_skinny_splits(args.tiles, args.k_blocks, d.sms, M, N, K);
   args.kb_per_split = (int)ceil_div(args.k_blocks, splits);
   args.splits = (int)ceil_div(args.k_blocks, args.kb_per_split);
   args.status = d.status;
