@@ -22,7 +22,8 @@ import types
 
 from . import capi  # noqa: F401
 
-__all__ = ["module", "matmul_b200", "profile_matmul_b200", "profile_rows", "capi", "load"]
+__all__ = ["module", "matmul_b200", "profile_matmul_b200", "matmul_b200_epilogue", "profile_rows",
+           "capi", "load"]
 
 _ext = None
 
@@ -54,6 +55,64 @@ def profile_matmul_b200(A, B, profiler, num_entries: int):
     CUDA tensor with at least ``profile_rows(M, N, K) * (1 + 4 * num_entries)``
     elements (see ``blackwell_gemm_b200.profiler``)."""
     return load().profile_matmul_b200(A, B, profiler, int(num_entries))
+
+
+def _row_major(t):
+    """Row-major view with a 16-byte aligned row stride (copies if needed)."""
+    rows, cols = t.shape
+    ok = (cols <= 1 or t.stride(1) == 1) and (rows <= 1 or (t.stride(0) % 8 == 0 and
+                                                           t.stride(0) >= cols))
+    if ok and t.data_ptr() % 16 == 0:
+        return t, (t.stride(0) if rows > 1 else (cols + 7) // 8 * 8)
+    import torch
+    ld = (cols + 7) // 8 * 8
+    buf = torch.empty(rows, ld, dtype=t.dtype, device=t.device)
+    buf[:, :cols].copy_(t)
+    return buf[:, :cols], ld
+
+
+def matmul_b200_epilogue(A, B, *, alpha: float = 1.0, bias=None, beta: float = 1.0,
+                         residual=None):
+    """C = round_bf16(alpha * (A @ B) + bias + beta * residual) in one pass.
+
+    A: (M, K) bf16 CUDA; B: (K, N) bf16 CUDA (the (K, N) view of an N x K
+    buffer, as for matmul_b200); bias: (N,) bf16 or None; residual: (M, N)
+    bf16 or None.  Accumulation and the epilogue arithmetic are fp32; the
+    result is rounded to bf16 once."""
+    import torch
+
+    if A.dim() != 2 or B.dim() != 2 or B.shape[0] != A.shape[1]:
+        raise RuntimeError("matmul_b200_epilogue: A must be (M, K) and B (K, N)")
+    for t in (A, B) + tuple(x for x in (bias, residual) if x is not None):
+        if not t.is_cuda or t.dtype != torch.bfloat16 or t.device != A.device:
+            raise RuntimeError("matmul_b200_epilogue: operands must be bfloat16 CUDA tensors "
+                               "on one device")
+    M, K = A.shape
+    N = B.shape[1]
+    a, lda = _row_major(A)
+    bt, ldb = _row_major(B.t())
+    ldc = (N + 7) // 8 * 8
+    Cbuf = torch.empty(M, ldc, dtype=torch.bfloat16, device=A.device)
+    bias_ptr = 0
+    if bias is not None:
+        if bias.shape != (N,):
+            raise RuntimeError("matmul_b200_epilogue: bias must have shape (N,)")
+        bias = bias.contiguous()
+        if bias.data_ptr() % 16:
+            bias = bias.clone()
+        bias_ptr = bias.data_ptr()
+    resid_ptr, ldr = 0, 0
+    if residual is not None:
+        if residual.shape != (M, N):
+            raise RuntimeError("matmul_b200_epilogue: residual must have shape (M, N)")
+        residual, ldr = _row_major(residual)
+        resid_ptr = residual.data_ptr()
+    with torch.cuda.device(A.device):
+        st = capi.gemm_bf16_epilogue(a.data_ptr(), bt.data_ptr(), Cbuf.data_ptr(), M, N, K, lda,
+                                     ldb, ldc, alpha, bias_ptr, beta, resid_ptr, ldr,
+                                     torch.cuda.current_stream(A.device).cuda_stream)
+    capi.check(st, "matmul_b200_epilogue")
+    return Cbuf[:, :N] if ldc == N else Cbuf[:, :N].contiguous()
 
 
 def profile_rows(M: int, N: int, K: int) -> int:

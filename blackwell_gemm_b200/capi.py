@@ -41,6 +41,8 @@ SIGNATURES = {
     "b200_gemm_bf16_f32out": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "b200_gemm_bf16_noalloc": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "b200_cast_f32_bf16": (_i, [_vp, _i, _vp, _i, _i, _i, _vp]),
+    "b200_gemm_bf16_epilogue": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, ctypes.c_float, _vp,
+                                     ctypes.c_float, _vp, _i, _vp]),
     "b200_gemm_set_splits": (_i, [_i]),
     "b200_gemm_get_splits": (_i, [_i, _i, _i, _ip]),
     "b200_gemm_profile_rows": (_i, [_i, _i, _i, _ip]),
@@ -98,6 +100,14 @@ def gemm_bf16_f32out(a_ptr: int, b_ptr: int, c_ptr: int, M: int, N: int, K: int,
                      ldb: int, ldc: int, stream: int = 0) -> int:
     """fp32 C = A * B^T (no rounding); ldc in floats.  Returns the status."""
     return lib().b200_gemm_bf16_f32out(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, stream)
+
+
+def gemm_bf16_epilogue(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, alpha, bias_ptr, beta,
+                       resid_ptr, ldr, stream=0) -> int:
+    """C = round(alpha A B^T + bias + beta R); bias_ptr / resid_ptr may be 0."""
+    return lib().b200_gemm_bf16_epilogue(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc,
+                                         float(alpha), bias_ptr or None, float(beta),
+                                         resid_ptr or None, ldr, stream)
 
 
 def cast_f32_bf16(w_ptr: int, ldw: int, c_ptr: int, ldc: int, M: int, N: int,

@@ -235,7 +235,8 @@ int init_device(DeviceState& d, int dev) {
   d.sms = prop.multiProcessorCount;
   if (!set_smem_limits<kV256x64>() || !set_smem_limits<kV256x128>() ||
       !set_smem_limits<kV512x64>() || !set_smem_limit<false, kV256x64, kOutF32>() ||
-      !set_smem_limit<false, kV256x64, kOutF32Add>() || !set_skinny_limits())
+      !set_smem_limit<false, kV256x64, kOutF32Add>() ||
+      !set_smem_limit<false, kV256x64, kOutBf16Epi>() || !set_skinny_limits())
     return B200_ERR_LAUNCH;
   if (query_pairs<kV256x64>(d.sms, &d.max_pairs[kV256x64]) != B200_OK ||
       query_pairs<kV256x128>(d.sms, &d.max_pairs[kV256x128]) != B200_OK ||
@@ -386,12 +387,13 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
 
 
 int cast_to_bf16(const float* W, int ldw, void* C, int ldc, int M, int N, int sms,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, const EpiArgs* epi = nullptr) {
+  const EpiArgs none = {1.0f, 0.0f, nullptr, nullptr, 0};
   const long long groups = (long long)M * ((N + 7) / 8);
   long long blocks = ceil_div(groups, 256);
   if (blocks > 8LL * sms) blocks = 8LL * sms;
   cast_f32_to_bf16_kernel<<<(int)blocks, 256, 0, stream>>>(
-      W, ldw, static_cast<__nv_bfloat16*>(C), ldc, M, N);
+      W, ldw, static_cast<__nv_bfloat16*>(C), ldc, M, N, epi ? *epi : none, epi != nullptr);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
 }
 
@@ -422,7 +424,7 @@ constexpr int kSkinnyMaxM = 256;
 
 template <int kMp, int kSlabs>
 int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
-                  int ldc, DeviceState& d, cudaStream_t stream) {
+                  int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi) {
   using P = SkinnyCfg<kMp, kSlabs>;
   CUtensorMap tb, ta, tw;
   if (encode_2d(&tb, B, K, N, ldb, kSlabK, P::kRowsB) != B200_OK ||
@@ -456,28 +458,28 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
                                                                                 args);
     if (cudaGetLastError() != cudaSuccess) st = B200_ERR_LAUNCH;
   }
-  if (st == B200_OK) st = cast_to_bf16(W, ldw, C, ldc, M, N, d.sms, stream);
+  if (st == B200_OK) st = cast_to_bf16(W, ldw, C, ldc, M, N, d.sms, stream, epi);
   cudaFreeAsync(W, stream);
   return st;
 }
 
 template <int kSlabs>
 int run_skinny_slabs(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
-                     int ldc, DeviceState& d, cudaStream_t stream) {
+                     int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi) {
   if (M <= 16)
     return launch_skinny<16, skinny_fit_slabs(16, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
-                                                            stream);
+                                                            stream, epi);
   if (M <= 32)
     return launch_skinny<32, skinny_fit_slabs(32, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
-                                                            stream);
+                                                            stream, epi);
   if (M <= 64)
     return launch_skinny<64, skinny_fit_slabs(64, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
-                                                            stream);
+                                                            stream, epi);
   if (M <= 128)
     return launch_skinny<128, skinny_fit_slabs(128, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
-                                                              stream);
+                                                              stream, epi);
   return launch_skinny<256, skinny_fit_slabs(256, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
-                                                            stream);
+                                                            stream, epi);
 }
 
 // K slabs per stage of the skinny kernel (B200_GEMM_SKINNY_SLABS: 1, 2, 4).
@@ -562,16 +564,19 @@ int run_skinny_cluster(const void* A, const void* B, void* C, int M, int N, int 
 }
 
 int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
-               int ldc, DeviceState& d, cudaStream_t stream) {
+               int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi = nullptr) {
   // Up to 16 rows of A the single-launch cluster kernel is faster (no
   // workspace clear or rounding pass); above, the persistent kernel streams
   // better.  B200_GEMM_SKINNY=2 forces the cluster kernel for every M.
   static const int mode = env_int("B200_GEMM_SKINNY", 1, 0, 2);
-  if (mode == 2 || M <= 16) return run_skinny_cluster(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
+  // (The cluster kernel writes C directly, so fused epilogues take the
+  // workspace kernel, whose rounding pass applies them.)
+  if (epi == nullptr && (mode == 2 || M <= 16))
+    return run_skinny_cluster(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
   switch (skinny_slabs()) {
-    case 1: return run_skinny_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
-    case 4: return run_skinny_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
-    default: return run_skinny_slabs<2>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
+    case 1: return run_skinny_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
+    case 4: return run_skinny_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
+    default: return run_skinny_slabs<2>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
   }
 }
 
@@ -597,12 +602,14 @@ GemmArgs base_args(int M, int N, int K, const DeviceState& d, long long* prof, i
   args.timeout_ns = g_timeout_ns.load();
   args.prof = prof;
   args.prof_entries = entries;
+  args.epi = {1.0f, 0.0f, nullptr, nullptr, 0};
   return args;
 }
 
 template <bool kProfile>
 int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
-             int ldc, long long* prof, int prof_entries, cudaStream_t stream) {
+             int ldc, long long* prof, int prof_entries, cudaStream_t stream,
+             const EpiArgs* epi = nullptr) {
   int st = validate(A, B, C, M, N, K, lda, ldb, ldc);
   if (st != B200_OK) return st;
   if (M == 0 || N == 0) return B200_OK;
@@ -623,8 +630,9 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda
     return B200_ERR_TENSOR_MAP;
 
   if (!kProfile && use_skinny(M, N, K))
-    return run_skinny(A, B, C, M, N, K, lda, ldb, ldc, *d, stream);
+    return run_skinny(A, B, C, M, N, K, lda, ldb, ldc, *d, stream, epi);
   GemmArgs args = base_args(M, N, K, *d, prof, prof_entries);
+  if (epi) args.epi = *epi;
   // Split-K (not with the profiler): tiles accumulate their K slices into a
   // zeroed fp32 workspace by TMA reduce-add, then one pass rounds to bf16.
   if (!kProfile) {
@@ -644,11 +652,12 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda
         st = B200_ERR_LAUNCH;
       if (st == B200_OK) st = launch<false, kV256x64, kOutF32Add>(ta, tb, tc, args, splits, *d,
                                                                    stream);
-      if (st == B200_OK) st = cast_to_bf16(W, ldw, C, ldc, M, N, d->sms, stream);
+      if (st == B200_OK) st = cast_to_bf16(W, ldw, C, ldc, M, N, d->sms, stream, epi);
       cudaFreeAsync(W, stream);
       return st;
     }
   }
+  if (!kProfile && epi) return launch<false, kV256x64, kOutBf16Epi>(ta, tb, tc, args, 1, *d, stream);
   switch (choose_variant(M, N, d->max_pairs)) {
     case kV256x128: return launch<kProfile, kV256x128, kOutBf16>(ta, tb, tc, args, 1, *d, stream);
     case kV512x64: return launch<kProfile, kV512x64, kOutBf16>(ta, tb, tc, args, 1, *d, stream);
@@ -705,6 +714,18 @@ int b200_gemm_bf16_profile(const void* A, const void* B, void* C, int M, int N, 
 int b200_gemm_bf16_f32out(const void* A, const void* B, float* C, int M, int N, int K, int lda,
                           int ldb, int ldc, void* stream) {
   return run_gemm_f32out(A, B, C, M, N, K, lda, ldb, ldc, static_cast<cudaStream_t>(stream));
+}
+
+int b200_gemm_bf16_epilogue(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                            int ldb, int ldc, float alpha, const void* bias, float beta,
+                            const void* residual, int ldr, void* stream) {
+  if (bias && !aligned16(bias)) return B200_ERR_ALIGNMENT;
+  if (residual && (!aligned16(residual) || (ldr & 7))) return B200_ERR_ALIGNMENT;
+  if (residual && ldr < N) return B200_ERR_INVALID_ARGUMENT;
+  const EpiArgs epi = {alpha, beta, static_cast<const __nv_bfloat16*>(bias),
+                       static_cast<const __nv_bfloat16*>(residual), ldr};
+  return run_gemm<false>(A, B, C, M, N, K, lda, ldb, ldc, nullptr, 0,
+                         static_cast<cudaStream_t>(stream), &epi);
 }
 
 int b200_cast_f32_bf16(const float* W, int ldw, void* C, int ldc, int M, int N, void* stream) {

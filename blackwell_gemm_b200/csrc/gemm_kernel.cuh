@@ -36,6 +36,13 @@
 
 namespace b200 {
 
+struct EpiArgs {
+  float alpha, beta;
+  const __nv_bfloat16* bias;   // N values (or null)
+  const __nv_bfloat16* resid;  // M x N, row stride ldr (or null)
+  int ldr;
+};
+
 struct GemmArgs {
   int M, N, K;
   int tiles_m, tiles_n, k_blocks, group;
@@ -45,6 +52,9 @@ struct GemmArgs {
   unsigned long long timeout_ns;  // bound on any single pipeline wait
   long long* prof;                // intra-kernel profiler rows (nullptr: off)
   int prof_entries;
+  // Fused epilogue (kOutBf16Epi): C = round(alpha acc + bias[n] + beta R[m][n]);
+  // bias and resid may be null, resid may alias C.
+  EpiArgs epi;
 };
 
 // Error codes written to GemmArgs::status by a wait that ran out.
@@ -139,6 +149,50 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, cons
   return wait_slow(bar, parity, w, code, true);
 }
 
+// In place on 32 consecutive accumulator columns of one row (fp32 bits):
+// v = alpha v + bias[col..] + beta resid[row][col..].  Rows >= M and columns
+// >= N are left as they are (the store clips them).  Bias and residual rows
+// are read with 16-byte loads (both are 16-byte aligned by contract).
+__device__ __forceinline__ void epi_apply(uint32_t (&v)[32], const EpiArgs& e, int M, int N,
+                                          int row, int col) {
+  float f[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) f[j] = e.alpha * __uint_as_float(v[j]);
+  const bool full = col + 32 <= N;
+  auto add8 = [&](const __nv_bfloat16* p, int j0, float scale) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      f[j0 + 2 * q] += scale * __uint_as_float(w[q] << 16);
+      f[j0 + 2 * q + 1] += scale * __uint_as_float(w[q] & 0xFFFF0000u);
+    }
+  };
+  if (e.bias != nullptr) {
+    if (full) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) add8(e.bias + col + 8 * q, 8 * q, 1.0f);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col + j < N) f[j] += __bfloat162float(e.bias[col + j]);
+    }
+  }
+  if (e.resid != nullptr && row < M) {
+    const __nv_bfloat16* r = e.resid + (long long)row * e.ldr + col;
+    if (full) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) add8(r + 8 * q, 8 * q, e.beta);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col + j < N) f[j] += e.beta * __bfloat162float(r[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(f[j]);
+}
+
 // Work unit u -> tile (tm, tn) and its K-block range [kb0, kb1).
 __device__ __forceinline__ void unit_coord(int u, const GemmArgs& a, int* tm, int* tn, int* kb0,
                                            int* kb1) {
@@ -162,7 +216,8 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_c,
                       const GemmArgs args) {
   using P = Cfg<kSlabs, kNSub>;
-  static_assert(kOut == kOutBf16 || kNSub == 1, "fp32 outputs use 256-wide pair tiles");
+  static_assert(kOut == kOutBf16 || kNSub == 1,
+                "fp32 outputs and fused epilogues use 256-wide pair tiles");
   constexpr int kStages = P::kStages;
   constexpr int kAccBufs = P::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
@@ -369,7 +424,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       // Row `lane` of a 32x64 box is 8 chunks of 16 B; chunk j is stored at
       // position j ^ (row % 8) -- the TMA 128 B swizzle pattern.
       const uint32_t row_off = lane * 128u;
-      if constexpr (kOut != kOutBf16) {
+      if constexpr (kOut == kOutF32 || kOut == kOutF32Add) {
         // fp32: 8 chunks of 32 columns (128 B rows); chunk j of 16 B at
         // position j ^ (row % 8), as above.
 #pragma unroll 1
@@ -407,6 +462,10 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           tmem_ld_32x32b_x32(tbase + c * kStoreCols, v0);
           tmem_ld_32x32b_x32(tbase + c * kStoreCols + 32, v1);
           tmem_wait_ld();
+          if constexpr (kOut == kOutBf16Epi) {
+            epi_apply(v0, args.epi, args.M, args.N, row0 + lane, col0 + c * kStoreCols);
+            epi_apply(v1, args.epi, args.M, args.N, row0 + lane, col0 + c * kStoreCols + 32);
+          }
           if (c == kSubN / kStoreCols - 1) {
             // All of this warp's part of the buffer is in registers: hand
             // TMEM back to the MMA.
@@ -514,9 +573,9 @@ __global__ void __cluster_dims__(2, 1, 1) wait_probe_kernel(int* status,
 // nearest even.  Eight columns per thread; vector loads and stores when the
 // row has eight columns left and both rows are 16-byte aligned there.
 __global__ void __launch_bounds__(256) cast_f32_to_bf16_kernel(const float* __restrict__ W,
-                                                               int ldw,
-                                                               __nv_bfloat16* __restrict__ C,
-                                                               int ldc, int M, int N) {
+                                                               int ldw, __nv_bfloat16* C,
+                                                               int ldc, int M, int N,
+                                                               EpiArgs epi, bool fused) {
   const int groups = (N + 7) / 8;
   const long long total = (long long)M * groups;
   for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < total;
@@ -525,17 +584,33 @@ __global__ void __launch_bounds__(256) cast_f32_to_bf16_kernel(const float* __re
     const int col = (int)(g - (long long)row * groups) * 8;
     const float* w = W + (long long)row * ldw + col;
     __nv_bfloat16* c = C + (long long)row * ldc + col;
-    if (col + 8 <= N) {
+    const int n_here = N - col < 8 ? N - col : 8;
+    float f[8];
+    if (n_here == 8) {
       const float4 a = *reinterpret_cast<const float4*>(w);
       const float4 b = *reinterpret_cast<const float4*>(w + 4);
+      f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+      f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    } else {
+      for (int i = 0; i < 8; ++i) f[i] = i < n_here ? w[i] : 0.f;
+    }
+    if (fused) {
+      // the same arithmetic as epi_apply: alpha acc + bias + beta resid
+      for (int i = 0; i < n_here; ++i) {
+        f[i] *= epi.alpha;
+        if (epi.bias) f[i] += __bfloat162float(epi.bias[col + i]);
+        if (epi.resid) f[i] += epi.beta * __bfloat162float(epi.resid[(long long)row * epi.ldr + col + i]);
+      }
+    }
+    if (n_here == 8) {
       uint4 o;
-      o.x = pack_bf16x2(__float_as_uint(a.x), __float_as_uint(a.y));
-      o.y = pack_bf16x2(__float_as_uint(a.z), __float_as_uint(a.w));
-      o.z = pack_bf16x2(__float_as_uint(b.x), __float_as_uint(b.y));
-      o.w = pack_bf16x2(__float_as_uint(b.z), __float_as_uint(b.w));
+      o.x = pack_bf16x2(__float_as_uint(f[0]), __float_as_uint(f[1]));
+      o.y = pack_bf16x2(__float_as_uint(f[2]), __float_as_uint(f[3]));
+      o.z = pack_bf16x2(__float_as_uint(f[4]), __float_as_uint(f[5]));
+      o.w = pack_bf16x2(__float_as_uint(f[6]), __float_as_uint(f[7]));
       *reinterpret_cast<uint4*>(c) = o;
     } else {
-      for (int i = 0; col + i < N; ++i) c[i] = __float2bfloat16_rn(w[i]);
+      for (int i = 0; i < n_here; ++i) c[i] = __float2bfloat16_rn(f[i]);
     }
   }
 }

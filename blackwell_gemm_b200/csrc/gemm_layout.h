@@ -41,6 +41,7 @@ enum OutMode : int {
   kOutBf16 = 0,    // C bf16 = round(acc)                    (the GEMM)
   kOutF32 = 1,     // C fp32 = acc                           (K-split partials)
   kOutF32Add = 2,  // C fp32 += acc, by TMA reduce-add       (split-K workspace)
+  kOutBf16Epi = 3, // C bf16 = round(alpha acc + bias[n] + beta R[m][n])
 };
 
 // Kernel configuration.

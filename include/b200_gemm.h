@@ -52,6 +52,16 @@ int b200_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, i
 int b200_gemm_bf16_f32out(const void* A, const void* B, float* C, int M, int N, int K, int lda,
                           int ldb, int ldc, void* stream);
 
+/* C = round(alpha * (A * B^T) + bias[n] + beta * R[m][n]) in one pass: the
+ * fused epilogue of a transformer projection (scale, bias, residual add),
+ * rounded to bf16 once.  bias: N bf16 values or NULL; residual R: M x N bf16
+ * with row stride ldr (a multiple of 8) or NULL, and may be C itself; both
+ * 16-byte aligned.  Other requirements as b200_gemm_bf16.  No reference
+ * counterpart: the reference's epilogue only converts. */
+int b200_gemm_bf16_epilogue(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                            int ldb, int ldc, float alpha, const void* bias, float beta,
+                            const void* residual, int ldr, void* stream);
+
 /* bf16 C = round-to-nearest-even(W) for an fp32 M x N matrix W (row stride
  * ldw floats, a multiple of 4; C row stride ldc, a multiple of 8).  The last
  * step of a K-split GEMM after the partials are summed.  No reference
