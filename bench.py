@@ -425,9 +425,13 @@ def main():
 
 def run_ksplit(args, world, rank, dev):
     """Configuration 5b: C = A B^T with M = N = 8192 and K = 131072 split
-    across the ranks (strong scaling).  One step = this rank's fp32 partial
-    (our kernel, b200_gemm_bf16_f32out) + NCCL reduce-scatter (sum) + bf16
-    cast of this rank's rows, all inside the CUDA events; max over ranks."""
+    across the ranks (strong scaling).  One step of the headline arm = one
+    fused kernel per rank (b200_ksplit_gemm_bf16: this rank's K-slice, the
+    other owners' fp32 tiles written into their memory over NVLink while it
+    computes, its own rows summed and rounded in the epilogue).  The unfused
+    sequence -- fp32 partial (b200_gemm_bf16_f32out), NCCL reduce-scatter
+    (sum), bf16 cast -- is timed the same way beside it.  CUDA events around
+    each step, max over ranks."""
     import torch.distributed as dist
     from datetime import timedelta
     if world > 1:
@@ -441,49 +445,83 @@ def run_ksplit(args, world, rank, dev):
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
     group = dist.group.WORLD if world > 1 else None
+    fused = bdist.FusedKSplit(M, N, group)
+    out = torch.empty(M // world, N, dtype=torch.bfloat16, device=dev)
 
-    def step():
+    def step_fused():
+        return fused(A, Bt, out)
+
+    def step_nccl():
         partial = bdist.gemm_f32_cuda(A, Bt)
         if world > 1:
-            out = torch.empty(M // world, N, dtype=torch.float32, device=dev)
-            dist.reduce_scatter_tensor(out, partial, op=dist.ReduceOp.SUM, group=group)
+            rs = torch.empty(M // world, N, dtype=torch.float32, device=dev)
+            dist.reduce_scatter_tensor(rs, partial, op=dist.ReduceOp.SUM, group=group)
         else:
-            out = partial
-        return bdist.cast_bf16_cuda(out)
+            rs = partial
+        return bdist.cast_bf16_cuda(rs)
 
-    step()
-    torch.cuda.synchronize()
-    time.sleep(IDLE_BEFORE_ARM_S)
-    for _ in range(args.warmup):
-        flush.zero_()
+    def timed(step):
         step()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    starts, ends = cold_l2_loop(step, args.steps, stream, flush)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
-    t = torch.tensor([sum(ms)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t[0])
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        time.sleep(IDLE_BEFORE_ARM_S)
+        for _ in range(args.warmup):
+            flush.zero_()
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        starts, ends = cold_l2_loop(step, args.steps, stream, flush)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+        t = torch.tensor([sum(ms)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0]), ms
+
+    # The unfused sequence first, then the fused kernel (headline).
+    nccl_ms, _ = timed(step_nccl)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    total_ms, ms = timed(step_fused)
+    clocks.stop()
+    clk = clocks.report()
+    from blackwell_gemm_b200 import capi
+    status = capi.device_status(True)
+    fused.close()
     flops = 2 * M * N * K
+    tf = flops * args.steps / (total_ms * 1e-3) / 1e12
+    peaks, src = measured_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_BF16_TFLOPS))
+    # fp32 bytes each rank sends over NVLink per step: (P-1)/P of its M x N partial
+    link_bytes = (world - 1) * (M // world) * N * 4
     if rank == 0:
         print(json.dumps({
             "metric": "BF16 GEMM TFLOP/s (cold-L2), K-split 8192 x 8192 x 131072",
-            "value": flops * args.steps / (total_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "value": tf, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "K-split GEMM: per-rank fp32 partial, NCCL reduce-scatter "
-                                   "(sum) over NVLink, bf16 cast",
+            "config": {"workload": "K-split GEMM, fused: per-rank K-slice GEMM whose epilogue "
+                                   "sends other owners' fp32 tiles over NVLink and sums + "
+                                   "rounds its own rows (one kernel per rank)",
                        "M": M, "N": N, "K": K, "k_per_gpu": Kr,
                        "l2": "flushed: 256 MB written before every step",
                        "parallelism": f"k-split{world}"},
-            "step_ms": step_stats(ms), "impl": "ours", "gpu_launches": 2 * args.steps,
-            "parity": "tests/test_splitk_gpu.py::test_k_split_and_row_shard_on_two_gpus",
+            "roofline": {"bound": "tensor", "achieved": tf / world, "peak": peak,
+                         "unit": "TFLOP/s", "frac": tf / world / peak,
+                         "peak_source": src, "per": "GPU",
+                         "nvlink_bytes_per_rank_per_step": link_bytes},
+            "unfused_nccl": {"value": flops * args.steps / (nccl_ms * 1e-3) / 1e12,
+                             "ms_per_step": nccl_ms / args.steps,
+                             "what": "b200_gemm_bf16_f32out + NCCL reduce_scatter_tensor(sum) "
+                                     "+ b200_cast_f32_bf16"},
+            "clocks": clk, "device_status": status,
+            "step_ms": step_stats(ms), "impl": "ours", "gpu_launches": args.steps,
+            "parity": "tests/test_ksplit_fused_gpu.py",
         }), flush=True)
     if world > 1:
         dist.barrier()

@@ -60,7 +60,8 @@ def _run(cmd, verbose: bool) -> str:
 
 def build_lib(force: bool = False, verbose: bool = False) -> Path:
     srcs = [CSRC / "gemm_capi.cu", CSRC / "gemm_kernel.cuh", CSRC / "gemm_layout.h",
-            CSRC / "sm100_ptx.cuh", INCLUDE / "b200_gemm.h"]
+            CSRC / "gemm_skinny.cuh", CSRC / "ksplit_fused.cuh", CSRC / "sm100_ptx.cuh",
+            INCLUDE / "b200_gemm.h"]
     if not force and not _stale(LIB, srcs):
         return LIB
     tmp = LIB.with_suffix(".so.tmp")

@@ -29,7 +29,10 @@ DEVICE_WAIT_CODES = {
     0x1004: "epilogue wait on the MMA",
     0x1005: "final MMA drain",
     0x1006: "wait probe",
+    0x1007: "K-split: a peer's piece of an own tile never arrived",
 }
+
+KSPLIT_HANDLE_BYTES = 128
 
 # Every symbol the header declares, with (restype, argtypes).
 _vp, _i, _u32, _u64, _ull = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, \
@@ -56,6 +59,11 @@ SIGNATURES = {
     "b200_gemm_idesc": (_u32, [_i, _i]),
     "b200_gemm_smem_desc": (_u64, [_u32]),
     "b200_gemm_launch_shape": (_i, [_i, _i, _i, _ip, _ip, _ip, _ip]),
+    "b200_ksplit_create": (_i, [_i, _i, _i, _i, ctypes.POINTER(_vp), _vp]),
+    "b200_ksplit_connect": (_i, [_vp, _vp]),
+    "b200_ksplit_gemm_bf16": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "b200_ksplit_epoch": (_i, [_vp, ctypes.POINTER(ctypes.c_uint)]),
+    "b200_ksplit_destroy": (_i, [_vp]),
 }
 
 _lib = None
@@ -191,3 +199,34 @@ def launch_shape(M: int, N: int, K: int) -> dict:
     check(lib().b200_gemm_launch_shape(M, N, K, ctypes.byref(t), ctypes.byref(g), ctypes.byref(s),
                                        ctypes.byref(th)), "launch_shape")
     return {"tiles": t.value, "grid": g.value, "smem_bytes": s.value, "threads": th.value}
+
+
+# ------------------------------------------------- fused K-split over NVLink
+def ksplit_create(rank: int, nranks: int, max_m: int, max_n: int):
+    """(communicator handle, exchange bytes) for this rank on the current
+    device; raises GemmError on failure."""
+    comm = _vp()
+    buf = ctypes.create_string_buffer(KSPLIT_HANDLE_BYTES)
+    check(lib().b200_ksplit_create(rank, nranks, max_m, max_n, ctypes.byref(comm), buf),
+          "b200_ksplit_create")
+    return comm.value, buf.raw
+
+
+def ksplit_connect(comm: int, handles: bytes) -> None:
+    buf = ctypes.create_string_buffer(bytes(handles), len(handles))
+    check(lib().b200_ksplit_connect(comm, buf), "b200_ksplit_connect")
+
+
+def ksplit_gemm_bf16(comm: int, a_ptr: int, b_ptr: int, c_ptr: int, M: int, N: int, K: int,
+                     lda: int, ldb: int, ldc: int, stream: int = 0) -> int:
+    return lib().b200_ksplit_gemm_bf16(comm, a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, stream)
+
+
+def ksplit_epoch(comm: int) -> int:
+    e = ctypes.c_uint(0)
+    check(lib().b200_ksplit_epoch(comm, ctypes.byref(e)), "b200_ksplit_epoch")
+    return e.value
+
+
+def ksplit_destroy(comm: int) -> None:
+    check(lib().b200_ksplit_destroy(comm), "b200_ksplit_destroy")

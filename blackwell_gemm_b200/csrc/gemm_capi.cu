@@ -17,6 +17,7 @@
 
 #include <atomic>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "b200_gemm.h"
@@ -687,6 +688,104 @@ int run_gemm_f32out(const void* A, const void* B, float* C, int M, int N, int K,
   return launch<false, kV256x64, kOutF32>(ta, tb, tc, args, 1, *d, stream);
 }
 
+// ---------------------------------------------------------------------------
+// Fused K-split over NVLink (device side: ksplit_fused.cuh).
+//
+// Exchange blob (B200_KSPLIT_HANDLE_BYTES) that each rank publishes: the IPC
+// handle of its receive area plus what the peers check before mapping it.
+struct KsplitBlob {
+  uint32_t magic;
+  int32_t rank, nranks, device;
+  int64_t cap_pieces;
+  uint64_t bytes, flag_bytes;
+  cudaIpcMemHandle_t handle;
+};
+constexpr uint32_t kKsplitMagic = 0x4b533230u;  // "02SK"
+static_assert(sizeof(KsplitBlob) <= B200_KSPLIT_HANDLE_BYTES, "exchange blob too large");
+
+// Pieces (32 x 256 fp32 epilogue-warp slices) per owner for an M x N call.
+long long ks_pieces(long long M, long long N, int nranks) {
+  return M / nranks / kPairM * ceil_div(N, kSubN) * 8;
+}
+
+}  // namespace
+
+struct b200_ksplit_comm {
+  int device = -1, rank = 0, nranks = 1;
+  long long cap_pieces = 0;
+  size_t bytes = 0, flag_bytes = 0;
+  char* base = nullptr;                 // this rank's receive area
+  char* mapped[kMaxRanks] = {};         // every rank's receive area as mapped here
+  unsigned int epoch = 0;               // calls made so far
+  bool connected = false;
+};
+
+namespace {
+
+// Run `fn` with `dev` as the current device, restoring the caller's.
+template <class F>
+int on_device(int dev, F fn) {
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) {
+    cudaGetLastError();
+    return B200_ERR_UNSUPPORTED_DEVICE;
+  }
+  if (prev != dev && cudaSetDevice(dev) != cudaSuccess) {
+    cudaGetLastError();
+    return B200_ERR_UNSUPPORTED_DEVICE;
+  }
+  const int st = fn();
+  if (prev != dev) cudaSetDevice(prev);
+  return st;
+}
+
+int run_ksplit(b200_ksplit_comm* c, const void* A, const void* B, void* C, int M, int N, int K,
+               int lda, int ldb, int ldc, cudaStream_t stream) {
+  if (!c || !c->connected) return B200_ERR_INVALID_ARGUMENT;
+  if (M <= 0 || N <= 0 || K <= 0 || M % (kPairM * c->nranks) != 0) return B200_ERR_INVALID_ARGUMENT;
+  const int rows = M / c->nranks;
+  int st = validate(A, B, C, rows, N, K, lda, ldb, ldc);
+  if (st != B200_OK) return st;
+  const long long pieces = ks_pieces(M, N, c->nranks);
+  if (pieces > c->cap_pieces) return B200_ERR_TOO_LARGE;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != c->device) {
+    cudaGetLastError();
+    return B200_ERR_INVALID_ARGUMENT;
+  }
+  DeviceState* d = nullptr;
+  st = device_state(&d);
+  if (st != B200_OK) return st;
+  CUtensorMap ta, tb, tc;
+  if (encode_2d(&ta, A, K, M, lda, kSlabK, kCtaM) != B200_OK ||
+      encode_2d(&tb, B, K, N, ldb, kSlabK, kCtaN) != B200_OK ||
+      encode_2d(&tc, C, N, rows, ldc, kStoreCols, 32) != B200_OK)
+    return B200_ERR_TENSOR_MAP;
+  GemmArgs args = base_args(M, N, K, *d, nullptr, 0);
+  KsArgs& ks = args.ks;
+  ks.rank = c->rank;
+  ks.nranks = c->nranks;
+  ks.tiles_m_own = rows / kPairM;
+  ks.pieces = (int)pieces;
+  ks.epoch = c->epoch + 1;
+  ks.parity = (int)(ks.epoch & 1u);
+  // Peers may reach the call later than this rank (host skew, first-call
+  // set-up): their pieces get five times the pipeline's bound (10 s by
+  // default).
+  ks.peer_timeout_ns = 5ull * g_timeout_ns.load();
+  for (int q = 0; q < kMaxRanks; ++q) {
+    ks.recv[q] = nullptr;
+    ks.flags[q] = nullptr;
+  }
+  for (int q = 0; q < c->nranks; ++q) {
+    ks.flags[q] = reinterpret_cast<unsigned int*>(c->mapped[q]);
+    ks.recv[q] = reinterpret_cast<float*>(c->mapped[q] + c->flag_bytes);
+  }
+  st = launch<false, kV256x64, kOutKsplit>(ta, tb, tc, args, 1, *d, stream);
+  if (st == B200_OK) c->epoch = ks.epoch;  // the epoch is spent once the kernel is queued
+  return st;
+}
+
 template <int V>
 void shape_of(long long* tile_n, int* smem, int* threads) {
   using C = typename VariantCfg<V>::C;
@@ -856,6 +955,106 @@ void b200_gemm_tile_coord(int t, int tiles_m, int tiles_n, int group, int* tm, i
 uint32_t b200_gemm_idesc(int mma_m, int mma_n) { return make_idesc_bf16_f32(mma_m, mma_n); }
 
 uint64_t b200_gemm_smem_desc(uint32_t smem_addr) { return make_sdesc_k128(smem_addr); }
+
+int b200_ksplit_create(int rank, int nranks, int max_m, int max_n, b200_ksplit_comm** comm,
+                       void* handle) {
+  if (!comm || !handle) return B200_ERR_INVALID_ARGUMENT;
+  *comm = nullptr;
+  if (nranks < 1 || nranks > kMaxRanks || rank < 0 || rank >= nranks || max_n <= 0 ||
+      max_m <= 0 || max_m % (kPairM * nranks) != 0)
+    return B200_ERR_INVALID_ARGUMENT;
+  DeviceState* d = nullptr;
+  int st = device_state(&d);
+  if (st != B200_OK) return st;
+  if (!set_smem_limit<false, kV256x64, kOutKsplit>()) return B200_ERR_LAUNCH;
+  b200_ksplit_comm* c = new b200_ksplit_comm();
+  cudaGetDevice(&c->device);
+  c->rank = rank;
+  c->nranks = nranks;
+  c->cap_pieces = ks_pieces(max_m, max_n, nranks);
+  c->flag_bytes = (size_t)ceil_div((long long)nranks * c->cap_pieces * 4, 4096) * 4096;
+  c->bytes = c->flag_bytes + (size_t)2 * nranks * c->cap_pieces * kPieceFloats * sizeof(float);
+  KsplitBlob blob = {};
+  if (cudaMalloc(&c->base, c->bytes) != cudaSuccess ||
+      cudaMemset(c->base, 0, c->flag_bytes) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&blob.handle, c->base) != cudaSuccess) {
+    cudaGetLastError();
+    if (c->base) cudaFree(c->base);
+    delete c;
+    return B200_ERR_LAUNCH;
+  }
+  c->mapped[rank] = c->base;
+  blob.magic = kKsplitMagic;
+  blob.rank = rank;
+  blob.nranks = nranks;
+  blob.device = c->device;
+  blob.cap_pieces = c->cap_pieces;
+  blob.bytes = c->bytes;
+  blob.flag_bytes = c->flag_bytes;
+  std::memset(handle, 0, B200_KSPLIT_HANDLE_BYTES);
+  std::memcpy(handle, &blob, sizeof(blob));
+  *comm = c;
+  return B200_OK;
+}
+
+int b200_ksplit_connect(b200_ksplit_comm* c, const void* handles) {
+  if (!c || !handles || c->connected) return B200_ERR_INVALID_ARGUMENT;
+  const char* h = static_cast<const char*>(handles);
+  for (int q = 0; q < c->nranks; ++q) {
+    KsplitBlob b;
+    std::memcpy(&b, h + (size_t)q * B200_KSPLIT_HANDLE_BYTES, sizeof(b));
+    if (b.magic != kKsplitMagic || b.rank != q || b.nranks != c->nranks ||
+        b.cap_pieces != c->cap_pieces || b.bytes != c->bytes || b.flag_bytes != c->flag_bytes)
+      return B200_ERR_INVALID_ARGUMENT;
+  }
+  return on_device(c->device, [&]() {
+    for (int q = 0; q < c->nranks; ++q) {
+      if (q == c->rank) continue;
+      KsplitBlob b;
+      std::memcpy(&b, h + (size_t)q * B200_KSPLIT_HANDLE_BYTES, sizeof(b));
+      void* p = nullptr;
+      if (cudaIpcOpenMemHandle(&p, b.handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        for (int r = 0; r < q; ++r)
+          if (r != c->rank && c->mapped[r]) {
+            cudaIpcCloseMemHandle(c->mapped[r]);
+            c->mapped[r] = nullptr;
+          }
+        return B200_ERR_LAUNCH;
+      }
+      c->mapped[q] = static_cast<char*>(p);
+    }
+    c->connected = true;
+    return B200_OK;
+  });
+}
+
+int b200_ksplit_gemm_bf16(b200_ksplit_comm* comm, const void* A, const void* B, void* C, int M,
+                          int N, int K, int lda, int ldb, int ldc, void* stream) {
+  return run_ksplit(comm, A, B, C, M, N, K, lda, ldb, ldc, static_cast<cudaStream_t>(stream));
+}
+
+int b200_ksplit_epoch(const b200_ksplit_comm* comm, unsigned int* epoch) {
+  if (!comm || !epoch) return B200_ERR_INVALID_ARGUMENT;
+  *epoch = comm->epoch;
+  return B200_OK;
+}
+
+int b200_ksplit_destroy(b200_ksplit_comm* c) {
+  if (!c) return B200_OK;
+  const int st = on_device(c->device, [&]() {
+    int r = cudaDeviceSynchronize() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
+    for (int q = 0; q < c->nranks; ++q)
+      if (q != c->rank && c->mapped[q] && cudaIpcCloseMemHandle(c->mapped[q]) != cudaSuccess)
+        r = B200_ERR_LAUNCH;
+    if (c->base && cudaFree(c->base) != cudaSuccess) r = B200_ERR_LAUNCH;
+    cudaGetLastError();
+    return r;
+  });
+  delete c;
+  return st;
+}
 
 }  // extern "C"
 

@@ -32,6 +32,7 @@
 #include <stdint.h>
 
 #include "gemm_layout.h"
+#include "ksplit_fused.cuh"
 #include "sm100_ptx.cuh"
 
 namespace b200 {
@@ -55,6 +56,8 @@ struct GemmArgs {
   // Fused epilogue (kOutBf16Epi): C = round(alpha acc + bias[n] + beta R[m][n]);
   // bias and resid may be null, resid may alias C.
   EpiArgs epi;
+  // K-split exchange (kOutKsplit only): see ksplit_fused.cuh.
+  KsArgs ks;
 };
 
 // Error codes written to GemmArgs::status by a wait that ran out.
@@ -65,6 +68,7 @@ enum : int {
   kErrWaitAccFull = 0x1004,   // epilogue waited on the MMA
   kErrWaitDrain = 0x1005,     // final wait for outstanding MMAs
   kErrWaitProbe = 0x1006,     // self-test kernel (wait that nothing releases)
+  kErrWaitPeer = 0x1007,      // K-split: a peer's piece of an own tile never arrived
 };
 
 // Intra-kernel profiler tags; numbering and row format follow the
@@ -193,12 +197,94 @@ __device__ __forceinline__ void epi_apply(uint32_t (&v)[32], const EpiArgs& e, i
   for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(f[j]);
 }
 
-// Work unit u -> tile (tm, tn) and its K-block range [kb0, kb1).
+// K-split exchange: the whole (converged) warp waits until *flag, a word in
+// this GPU's memory that a peer raises, reaches `epoch`.  Every lane reads it
+// with acquire semantics at system scope, so each lane's later loads see the
+// peer's piece.  Gives up when the pair's abort word is set or after
+// timeout_ns (records kErrWaitPeer and raises both abort words); the verdict
+// is warp-uniform.
+__device__ __noinline__ bool wait_peer_flag(const unsigned int* flag, unsigned int epoch,
+                                            const WaitCtx& w, unsigned long long timeout_ns) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long t0 = 0;
+  for (int round = 0;; ++round) {
+    const bool ok = (int)(ld_acquire_sys_u32(flag) - epoch) >= 0;
+    if (__all_sync(0xffffffffu, ok)) return true;
+    int give_up = 0;
+    if (lane == 0) {
+      const unsigned long long now = globaltimer_ns();
+      if (round == 0) t0 = now;
+      if (ld_volatile_shared(w.abort_local) != 0) {
+        give_up = 1;
+      } else if (now - t0 > timeout_ns) {
+        atomicCAS(w.status, 0, kErrWaitPeer);
+        asm volatile("st.volatile.shared.u32 [%0], %1;" ::"r"(w.abort_local), "r"(1u) : "memory");
+        st_cluster_u32(w.abort_peer, 1u);
+        give_up = 1;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, give_up, 0)) return false;
+    __nanosleep(256);
+  }
+}
+
+// K-split exchange, own tile: v (fp32 bits of this rank's partial, columns
+// 32h..32h+31 of this lane's row) <- P_0 + P_1 + ... + P_{P-1}, summed left to
+// right in rank order.  `recv` points at this lane's float4 of source 0's
+// piece in this rank's receive slots; source q's piece is q * stride floats
+// further.
+__device__ __forceinline__ void ks_accumulate(uint32_t (&v)[32], const float* recv,
+                                              long long stride, int h, int rank, int nranks) {
+  float s[32];
+  auto add_src = [&](int q, bool first) {
+    const float* p = recv + q * stride + h * 8 * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 x = ld_global_cg_v4(p + j * 128);
+      if (first) {
+        s[4 * j] = x.x; s[4 * j + 1] = x.y; s[4 * j + 2] = x.z; s[4 * j + 3] = x.w;
+      } else {
+        s[4 * j] += x.x; s[4 * j + 1] += x.y; s[4 * j + 2] += x.z; s[4 * j + 3] += x.w;
+      }
+    }
+  };
+  if (rank == 0) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) s[j] = __uint_as_float(v[j]);
+  } else {
+    add_src(0, true);
+  }
+#pragma unroll 1
+  for (int q = 1; q < nranks; ++q) {
+    if (q == rank) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) s[j] += __uint_as_float(v[j]);
+    } else {
+      add_src(q, false);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(s[j]);
+}
+
+// Work unit u -> tile (tm, tn) and its K-block range [kb0, kb1).  In the
+// K-split exchange the tiles come in P phases, phase f over the rows of
+// owner (rank + 1 + f) mod P, each phase rastered like a whole grid.
+template <int kOut>
 __device__ __forceinline__ void unit_coord(int u, const GemmArgs& a, int* tm, int* tn, int* kb0,
                                            int* kb1) {
   const int t = u / a.splits;
   const int s = u - t * a.splits;
-  tile_coord(t, a.tiles_m, a.tiles_n, a.group, tm, tn);
+  if constexpr (kOut == kOutKsplit) {
+    const int own = a.ks.tiles_m_own * a.tiles_n;
+    const int phase = t / own;
+    int owner = a.ks.rank + 1 + phase;
+    if (owner >= a.ks.nranks) owner -= a.ks.nranks;
+    tile_coord(t - phase * own, a.ks.tiles_m_own, a.tiles_n, a.group, tm, tn);
+    *tm += owner * a.ks.tiles_m_own;
+  } else {
+    tile_coord(t, a.tiles_m, a.tiles_n, a.group, tm, tn);
+  }
   *kb0 = s * a.kb_per_split;
   const int end = *kb0 + a.kb_per_split;
   *kb1 = end < a.k_blocks ? end : a.k_blocks;
@@ -294,7 +380,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       bool ok = true;
       for (int u = pair; ok && u < units; u += npairs) {
         int tm, tn, kb0, kb1;
-        unit_coord(u, args, &tm, &tn, &kb0, &kb1);
+        unit_coord<kOut>(u, args, &tm, &tn, &kb0, &kb1);
         const int a_row = tm * kPairM + (int)rank * kCtaM;
         const int b_row = tn * P::kTileN + (int)rank * kCtaN;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -340,7 +426,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       bool ok = true;
       for (int u = pair; ok && u < units; u += npairs, ++it) {
         int tm, tn, kb0, kb1;
-        unit_coord(u, args, &tm, &tn, &kb0, &kb1);
+        unit_coord<kOut>(u, args, &tm, &tn, &kb0, &kb1);
         const uint32_t buf = it % kAccBufs, acc_phase = (it / kAccBufs) & 1;
         if constexpr (kProfile) prof.start(kTagWaitEpilogue);
         if (!wait_bounded(smem_u32(&bar_acc_empty[buf]), acc_phase ^ 1u, wctx, kErrWaitAccEmpty))
@@ -402,7 +488,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     int it = 0;
     for (int u = pair; u < units; u += npairs, ++it) {
       int tm, tn, kb0, kb1;
-      unit_coord(u, args, &tm, &tn, &kb0, &kb1);
+      unit_coord<kOut>(u, args, &tm, &tn, &kb0, &kb1);
       const uint32_t buf = it % kAccBufs, acc_phase = (it / kAccBufs) & 1;
       if constexpr (kProfile) {
         if (lane == 0) prof.start(kTagWaitMainloop);
@@ -456,6 +542,56 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           ++nstore;
         }
       } else if constexpr (kNSub == 1) {
+        int out_row = row0;             // first row of this warp's 32 in C
+        const float* recv = nullptr;    // K-split: own tile's received pieces
+        long long recv_stride = 0;
+        if constexpr (kOut == kOutKsplit) {
+          const KsArgs& ks = args.ks;
+          const int owner = tm / ks.tiles_m_own;
+          const long long piece =
+              ((long long)((tm - owner * ks.tiles_m_own) * args.tiles_n + tn) * 2 + (int)rank) *
+                  4 + quarter;
+          if (owner != ks.rank) {
+            // Another owner's tile: send this warp's piece into its receive
+            // slot, then raise the piece's flag there.
+            float* dst = ks.recv[owner] + ks_slot_offset(ks, ks.rank, piece) + 4 * lane;
+#pragma unroll 1
+            for (int c = 0; c < kSubN / 32; ++c) {
+              uint32_t v[32];
+              tmem_ld_32x32b_x32(tbase + c * 32, v);
+              tmem_wait_ld();
+              if (c == kSubN / 32 - 1) {
+                tc_fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(acc_empty_leader + buf * 8u);
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                st_global_v4(dst + (c * 8 + j) * 128, v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                             v[4 * j + 3]);
+            }
+            fence_acq_rel_sys();
+            __syncwarp();
+            if (lane == 0)
+              st_release_sys_u32(ks.flags[owner] + (long long)ks.rank * ks.pieces + piece,
+                                 ks.epoch);
+            if constexpr (kProfile) {
+              if (lane == 0) prof.stop();
+            }
+            continue;
+          }
+          // Own tile: every peer's piece must have arrived.
+          bool arrived = true;
+#pragma unroll 1
+          for (int q = 0; arrived && q < ks.nranks; ++q)
+            if (q != ks.rank)
+              arrived = wait_peer_flag(ks.flags[ks.rank] + (long long)q * ks.pieces + piece,
+                                       ks.epoch, wctx, ks.peer_timeout_ns);
+          if (!arrived) break;
+          recv = ks.recv[ks.rank] + ks_slot_offset(ks, 0, piece) + 4 * lane;
+          recv_stride = (long long)ks.pieces * kPieceFloats;
+          out_row = row0 - ks.rank * ks.tiles_m_own * kPairM;
+        }
 #pragma unroll 1
         for (int c = 0; c < kSubN / kStoreCols; ++c) {
           uint32_t v0[32], v1[32];
@@ -465,6 +601,10 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           if constexpr (kOut == kOutBf16Epi) {
             epi_apply(v0, args.epi, args.M, args.N, row0 + lane, col0 + c * kStoreCols);
             epi_apply(v1, args.epi, args.M, args.N, row0 + lane, col0 + c * kStoreCols + 32);
+          }
+          if constexpr (kOut == kOutKsplit) {
+            ks_accumulate(v0, recv, recv_stride, 2 * c, args.ks.rank, args.ks.nranks);
+            ks_accumulate(v1, recv, recv_stride, 2 * c + 1, args.ks.rank, args.ks.nranks);
           }
           if (c == kSubN / kStoreCols - 1) {
             // All of this warp's part of the buffer is in registers: hand
@@ -486,7 +626,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmap_c, sb, col0 + c * kStoreCols, row0);
+            tma_store_2d(&tmap_c, sb, col0 + c * kStoreCols, out_row);
             bulk_commit_group();
           }
           ++nstore;

@@ -42,6 +42,7 @@ enum OutMode : int {
   kOutF32 = 1,     // C fp32 = acc                           (K-split partials)
   kOutF32Add = 2,  // C fp32 += acc, by TMA reduce-add       (split-K workspace)
   kOutBf16Epi = 3, // C bf16 = round(alpha acc + bias[n] + beta R[m][n])
+  kOutKsplit = 4,  // K-split over ranks: peers' tiles sent, own rows summed + rounded
 };
 
 // Kernel configuration.

@@ -13,6 +13,11 @@ build is measured on:
   ``[r M/P, (r+1) M/P)``) and rank r rounds its rows to bf16 once
   (``b200_cast_f32_bf16``).  Rounding once after the sum keeps the result
   equal, up to fp32 summation order, to the single-GPU GEMM.
+* **Fused K-split** (``FusedKSplit``): the same decomposition in one kernel
+  per rank (``b200_ksplit_gemm_bf16``): each rank writes the fp32 tiles of
+  other owners' rows straight into the owner's memory over NVLink while it
+  computes, and adds the peers' tiles to its own rows in the epilogue, so the
+  exchange overlaps the tensor-core work and nothing is rounded twice.
 
 The local GEMM and the cast are arguments so the collective logic can be
 exercised on CPU ranks (``gloo``) with a plain fp32 GEMM; the GPU path always
@@ -85,6 +90,67 @@ def k_split_gemm(A_k: torch.Tensor, Bt_k: torch.Tensor, group: Optional[dist.Pro
     out = torch.empty(M // world, partial.shape[1], dtype=torch.float32, device=partial.device)
     dist.reduce_scatter_tensor(out, partial, op=dist.ReduceOp.SUM, group=group)
     return cast(out)
+
+
+class FusedKSplit:
+    """Rank's rows of C = A B^T from K-slices, reduced over NVLink inside the
+    GEMM kernel (``b200_ksplit_gemm_bf16``).
+
+    Construction is a collective over ``group`` (each rank on its own GPU,
+    the current device): every rank allocates its receive area for problems
+    up to ``max_m`` x ``max_n``, the IPC handles are all-gathered and mapped.
+    Calls are collectives too: every rank, same order, same M and N.
+    ``close()`` (also a collective) synchronizes, waits for every rank and
+    unmaps."""
+
+    def __init__(self, max_m: int, max_n: int, group: Optional[dist.ProcessGroup] = None):
+        from . import capi
+
+        self.group = group
+        # Without an initialised process group this is a one-rank instance.
+        self.collective = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if self.collective else 1
+        self.rank = dist.get_rank(group) if self.collective else 0
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.comm, handle = capi.ksplit_create(self.rank, self.world, max_m, max_n)
+        handles = [handle]
+        if self.collective:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle, group=group)
+        capi.ksplit_connect(self.comm, b"".join(handles))
+        if self.collective:
+            dist.barrier(group)
+
+    def __call__(self, A_k: torch.Tensor, Bt_k: torch.Tensor,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """A_k = A[:, Kr] (M x K_r), Bt_k = B[:, Kr] (N x K_r), both contiguous
+        bf16 on this rank's GPU; returns (or fills) rows [r M/P, (r+1) M/P)."""
+        from . import capi
+
+        if self.comm is None:
+            raise RuntimeError("FusedKSplit is closed")
+        M, K = A_k.shape
+        N = Bt_k.shape[0]
+        if not (A_k.is_contiguous() and Bt_k.is_contiguous()) or Bt_k.shape[1] != K:
+            raise ValueError("A_k (M x K_r) and Bt_k (N x K_r) must be contiguous")
+        if out is None:
+            out = torch.empty(M // self.world, N, dtype=torch.bfloat16, device=A_k.device)
+        st = capi.ksplit_gemm_bf16(self.comm, A_k.data_ptr(), Bt_k.data_ptr(), out.data_ptr(),
+                                   M, N, K, K, K, out.stride(0),
+                                   torch.cuda.current_stream(A_k.device).cuda_stream)
+        capi.check(st, "b200_ksplit_gemm_bf16")
+        return out
+
+    def close(self) -> None:
+        from . import capi
+
+        if self.comm is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.collective:
+            dist.barrier(self.group)
+        capi.ksplit_destroy(self.comm)
+        self.comm = None
 
 
 def k_slice(K: int, world: int, rank: int) -> slice:

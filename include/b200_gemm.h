@@ -148,6 +148,47 @@ const char* b200_gemm_status_string(int status);
 int b200_gemm_bf16_noalloc(const void* A, const void* B, void* C, int M, int N, int K, int lda,
                            int ldb, int ldc, void* stream);
 
+/* ---- Fused K-split over NVLink -------------------------------------------
+ * One GEMM C = A B^T (M x N x K) split along K over P ranks, one process per
+ * GPU: rank r holds A[:, K_r] (M x K_r) and B[:, K_r] (N x K_r) and receives
+ * the bf16 rows [r M/P, (r+1) M/P) of C.  It replaces the multi-GPU K-split
+ * sequence "fp32 partial (b200_gemm_bf16_f32out) -> collective
+ * reduce-scatter (sum) -> b200_cast_f32_bf16" with one kernel per rank: each
+ * rank computes the other owners' tiles first and writes their fp32
+ * accumulators straight into the owner's memory over NVLink (CUDA IPC
+ * mappings, plain stores), then computes its own tiles and adds the peers'
+ * contributions in its epilogue (sum in rank order, one rounding).  No
+ * reference counterpart (the reference is single-GPU); it is the fused form
+ * of the reduce-scatter + cast step of the K-split configuration.
+ *
+ * Set-up, once per group (a collective: every rank, same arguments but its
+ * own rank):
+ *   b200_ksplit_create(rank, P, max_m, max_n, &comm, handle)  on rank's GPU;
+ *       allocates 2 * max_m * round_up(max_n, 256) * 4 bytes plus flags and
+ *       writes B200_KSPLIT_HANDLE_BYTES of exchange data to `handle`;
+ *   all-gather the P handles (any transport, rank order);
+ *   b200_ksplit_connect(comm, handles)  maps every peer's area.
+ *   Every rank must return from connect before any rank calls the GEMM.
+ * Calls (a collective: every rank, same order, same M and N, K_r >= 1):
+ *   b200_ksplit_gemm_bf16(comm, A, B, C, M, N, K_r, lda, ldb, ldc, stream)
+ *       M a multiple of 256 P, M x N within the created capacity; C is this
+ *       rank's M/P x N block.  Asynchronous on `stream`; waits for peers are
+ *       on the device and bounded (5 x the pipeline wait bound, 10 s by default):
+ *       a missing peer sets the device error word (b200_gemm_device_status)
+ *       and the kernel returns.
+ * Tear-down: synchronize every rank's streams, barrier, then
+ *   b200_ksplit_destroy(comm). */
+#define B200_KSPLIT_HANDLE_BYTES 128
+typedef struct b200_ksplit_comm b200_ksplit_comm;
+int b200_ksplit_create(int rank, int nranks, int max_m, int max_n, b200_ksplit_comm** comm,
+                       void* handle);
+int b200_ksplit_connect(b200_ksplit_comm* comm, const void* handles);
+int b200_ksplit_gemm_bf16(b200_ksplit_comm* comm, const void* A, const void* B, void* C, int M,
+                          int N, int K, int lda, int ldb, int ldc, void* stream);
+/* Calls this communicator has queued so far (the epoch of the last one). */
+int b200_ksplit_epoch(const b200_ksplit_comm* comm, unsigned int* epoch);
+int b200_ksplit_destroy(b200_ksplit_comm* comm);
+
 /* Host-side layout rules, exported so they can be checked without a GPU. */
 void b200_gemm_tile_coord(int t, int tiles_m, int tiles_n, int group, int* tm, int* tn);
 uint32_t b200_gemm_idesc(int mma_m, int mma_n);

@@ -107,3 +107,17 @@ def test_torch_extension_builds_and_checks_inputs():
         bg.matmul_b200(a, a.T)
     with pytest.raises(RuntimeError, match="2-D"):
         bg.matmul_b200(a[0], a.T)
+
+
+def test_ksplit_rejects_bad_arguments_without_a_device():
+    for args in [(2, 2, 512, 256), (-1, 2, 512, 256), (0, 9, 4608, 256), (0, 2, 300, 256),
+                 (0, 1, 256, 0)]:
+        with pytest.raises(capi.GemmError) as e:
+            capi.ksplit_create(*args)
+        assert e.value.status == capi.ERR_INVALID_ARGUMENT, args
+    lib = capi.lib()
+    assert lib.b200_ksplit_gemm_bf16(None, FAKE, FAKE, FAKE, 512, 256, 64, 64, 64, 256,
+                                     None) == capi.ERR_INVALID_ARGUMENT
+    assert lib.b200_ksplit_connect(None, None) == capi.ERR_INVALID_ARGUMENT
+    assert lib.b200_ksplit_destroy(None) == capi.OK
+    assert capi.KSPLIT_HANDLE_BYTES == 128
