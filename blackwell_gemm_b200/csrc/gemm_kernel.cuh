@@ -267,6 +267,42 @@ __device__ __forceinline__ void ks_accumulate(uint32_t (&v)[32], const float* re
   for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(s[j]);
 }
 
+// K-split exchange: owner of 256-row tile tm and the index of the piece
+// (32 rows x 256 columns) that epilogue warp `quarter` of CTA `cta` holds for
+// 256-column block cb.
+__device__ __forceinline__ long long ks_piece(const KsArgs& ks, int tm, int cb, int cblocks,
+                                              int cta, int quarter, int* owner) {
+  *owner = tm / ks.tiles_m_own;
+  return ((long long)((tm - *owner * ks.tiles_m_own) * cblocks + cb) * 2 + cta) * 4 + quarter;
+}
+
+// K-split exchange, another owner's tile: write this warp's piece (TMEM
+// columns tbase .. tbase + 255, fp32) into `dst` (the owner's slot, piece
+// layout), hand the accumulator back after its last column, then raise
+// `flag` to `epoch` once every lane's stores are visible system-wide.
+__device__ __forceinline__ void ks_send_piece(uint32_t tbase, float* dst, unsigned int* flag,
+                                              unsigned int epoch, uint32_t acc_empty) {
+  const int lane = threadIdx.x & 31;
+  dst += 4 * lane;
+#pragma unroll 1
+  for (int c = 0; c < kSubN / 32; ++c) {
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(tbase + c * 32, v);
+    tmem_wait_ld();
+    if (c == kSubN / 32 - 1) {
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      st_global_v4(dst + (c * 8 + j) * 128, v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+  fence_acq_rel_sys();
+  __syncwarp();
+  if (lane == 0) st_release_sys_u32(flag, epoch);
+}
+
 // Work unit u -> tile (tm, tn) and its K-block range [kb0, kb1).  In the
 // K-split exchange the tiles come in P phases, phase f over the rows of
 // owner (rank + 1 + f) mod P, each phase rastered like a whole grid.
@@ -302,7 +338,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_c,
                       const GemmArgs args) {
   using P = Cfg<kSlabs, kNSub>;
-  static_assert(kOut == kOutBf16 || kNSub == 1,
+  static_assert(kOut == kOutBf16 || kOut == kOutKsplit || kNSub == 1,
                 "fp32 outputs and fused epilogues use 256-wide pair tiles");
   constexpr int kStages = P::kStages;
   constexpr int kAccBufs = P::kAccBufs;
@@ -547,34 +583,14 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
         long long recv_stride = 0;
         if constexpr (kOut == kOutKsplit) {
           const KsArgs& ks = args.ks;
-          const int owner = tm / ks.tiles_m_own;
-          const long long piece =
-              ((long long)((tm - owner * ks.tiles_m_own) * args.tiles_n + tn) * 2 + (int)rank) *
-                  4 + quarter;
+          int owner;
+          const long long piece = ks_piece(ks, tm, tn, args.tiles_n, (int)rank, quarter, &owner);
           if (owner != ks.rank) {
             // Another owner's tile: send this warp's piece into its receive
             // slot, then raise the piece's flag there.
-            float* dst = ks.recv[owner] + ks_slot_offset(ks, ks.rank, piece) + 4 * lane;
-#pragma unroll 1
-            for (int c = 0; c < kSubN / 32; ++c) {
-              uint32_t v[32];
-              tmem_ld_32x32b_x32(tbase + c * 32, v);
-              tmem_wait_ld();
-              if (c == kSubN / 32 - 1) {
-                tc_fence_before_sync();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(acc_empty_leader + buf * 8u);
-              }
-#pragma unroll
-              for (int j = 0; j < 8; ++j)
-                st_global_v4(dst + (c * 8 + j) * 128, v[4 * j], v[4 * j + 1], v[4 * j + 2],
-                             v[4 * j + 3]);
-            }
-            fence_acq_rel_sys();
-            __syncwarp();
-            if (lane == 0)
-              st_release_sys_u32(ks.flags[owner] + (long long)ks.rank * ks.pieces + piece,
-                                 ks.epoch);
+            ks_send_piece(tbase, ks.recv[owner] + ks_slot_offset(ks, ks.rank, piece),
+                          ks.flags[owner] + (long long)ks.rank * ks.pieces + piece, ks.epoch,
+                          acc_empty_leader + buf * 8u);
             if constexpr (kProfile) {
               if (lane == 0) prof.stop();
             }
@@ -632,6 +648,35 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           ++nstore;
         }
       } else {
+        int out_row = row0;
+        const float* recv = nullptr;
+        long long recv_stride = 0;
+        if constexpr (kOut == kOutKsplit) {
+          // As for 256-wide tiles, per 256-column sub-tile.
+          const KsArgs& ks = args.ks;
+          int owner;
+          const long long piece =
+              ks_piece(ks, tm, tn * kNSub + sub, args.tiles_n * kNSub, (int)rank, quarter, &owner);
+          if (owner != ks.rank) {
+            ks_send_piece(tbase, ks.recv[owner] + ks_slot_offset(ks, ks.rank, piece),
+                          ks.flags[owner] + (long long)ks.rank * ks.pieces + piece, ks.epoch,
+                          acc_empty_leader + buf * 8u);
+            if constexpr (kProfile) {
+              if (lane == 0) prof.stop();
+            }
+            continue;
+          }
+          bool arrived = true;
+#pragma unroll 1
+          for (int q = 0; arrived && q < ks.nranks; ++q)
+            if (q != ks.rank)
+              arrived = wait_peer_flag(ks.flags[ks.rank] + (long long)q * ks.pieces + piece,
+                                       ks.epoch, wctx, ks.peer_timeout_ns);
+          if (!arrived) break;
+          recv = ks.recv[ks.rank] + ks_slot_offset(ks, 0, piece) + 4 * lane;
+          recv_stride = (long long)ks.pieces * kPieceFloats;
+          out_row = row0 - ks.rank * ks.tiles_m_own * kPairM;
+        }
         // Drain this warp's 32 x 256 slice into registers as packed bf16
         // (128 registers per thread), release the accumulator, then store.
         uint32_t packed[kSubN / 2];
@@ -640,6 +685,8 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           uint32_t v[32];
           tmem_ld_32x32b_x32(tbase + c * 32, v);
           tmem_wait_ld();
+          if constexpr (kOut == kOutKsplit)
+            ks_accumulate(v, recv, recv_stride, c, args.ks.rank, args.ks.nranks);
 #pragma unroll
           for (int i = 0; i < 16; ++i) packed[c * 16 + i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
         }
@@ -659,7 +706,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmap_c, my_store, col0 + c * kStoreCols, row0);
+            tma_store_2d(&tmap_c, my_store, col0 + c * kStoreCols, out_row);
             bulk_commit_group();
           }
         }

@@ -1,13 +1,14 @@
 """Fused K-split over NVLink (b200_ksplit_* / distributed.FusedKSplit).
 
 * One rank (any single GPU): the communicator's kernel with P = 1 owns every
-  tile, so it must reproduce b200_gemm_bf16 bit for bit (same 256 x 256 pair
-  tiles, same MMA order) and the oracle exactly on exact-arithmetic inputs.
+  tile, so it must reproduce b200_gemm_bf16 bit for bit (same pair tiles, 256
+  or 512 wide, same MMA order) and the oracle exactly on exact-arithmetic
+  inputs.
 * Two ranks (two GPUs, one process each, NVLS off): rows must equal the
   NCCL reduce-scatter path bit for bit (same fp32 partials; a two-term fp32
   sum does not depend on order), match the oracle exactly on exact inputs and
   meet the parity bar on random ones, across several calls (both receive
-  parities) and a change of shape inside the capacity.  Then one rank calls
+  parities, both tile widths) and a change of shape inside the capacity.  Then one rank calls
   alone: its wait for the peer's pieces must run out (bound 5 x 0.2 s), set
   the device error word to 0x1007 and return.
 """
@@ -41,8 +42,10 @@ def _one_rank_call(comm, A, Bt, M, N, K):
     return C
 
 
-def test_single_rank_matches_gemm_and_oracle():
+@pytest.mark.parametrize("tile_n", [256, 512])
+def test_single_rank_matches_gemm_and_oracle(tile_n):
     comm, handle = capi.ksplit_create(0, 1, 1024, 1024)
+    capi.set_tuning(tile_n, 1, 0)
     try:
         capi.ksplit_connect(comm, handle)
         for M, N, K in [(1024, 1024, 1024), (512, 760, 1000), (256, 64, 64)]:
@@ -50,13 +53,11 @@ def test_single_rank_matches_gemm_and_oracle():
             C = _one_rank_call(comm, A, Bt, M, N, K)
             ref = torch.zeros(M, N, dtype=torch.bfloat16, device="cuda")
             capi.set_splits(1)
-            capi.set_tuning(256, 1, 0)
             try:
                 assert capi.gemm_bf16(A.data_ptr(), Bt.data_ptr(), ref.data_ptr(), M, N, K, K, K,
                                       N, 0) == capi.OK
             finally:
                 capi.set_splits(0)
-                capi.set_tuning(-1, 0, 0)
             torch.cuda.synchronize()
             assert torch.equal(C.view(torch.int16), ref.view(torch.int16)), (M, N, K)
             a, b = oracle.exact_inputs(M, N, K, seed=3)
@@ -64,6 +65,7 @@ def test_single_rank_matches_gemm_and_oracle():
             assert np.array_equal(_bits(C), oracle.gemm_bf16(a, b)), (M, N, K)
         assert capi.ksplit_epoch(comm) == 6
     finally:
+        capi.set_tuning(-1, 0, 0)
         capi.ksplit_destroy(comm)
     assert capi.device_status(True) == 0
 
@@ -118,9 +120,11 @@ def _worker(rank, world, port, q):
         report = []
         ok = True
         fk = bdist.FusedKSplit(2048, 1536)
-        # random operands, several calls: bits equal to the NCCL path, parity vs fp32
-        for call, (M, N, K) in enumerate([(2048, 1536, 4096), (2048, 1536, 4096),
-                                          (1024, 1000, 2048), (2048, 1536, 1024)]):
+        # random operands, several calls (256- then 512-wide pair tiles): bits
+        # equal to the NCCL path, parity against fp32
+        calls = [(2048, 1536, 4096), (2048, 1536, 4096), (1024, 1000, 2048), (2048, 1536, 1024)]
+        for call, (M, N, K) in enumerate(calls + calls):
+            capi.set_tuning(256 if call < len(calls) else 512, 1, 0)
             A, Bt = workloads.make_operands(M, N, K, seed=100 + call, device=dev)
             ks = bdist.k_slice(K, world, rank)
             Ak, Bk = A[:, ks].contiguous(), Bt[:, ks].contiguous()
@@ -132,6 +136,7 @@ def _worker(rank, world, port, q):
             same = torch.equal(rows.view(torch.int16), nccl_rows.view(torch.int16))
             ok &= parity.passes(m) and same
             report.append((call, M, N, K, same, m))
+        capi.set_tuning(-1, 0, 0)
         # exact inputs: bit-exact against the oracle (unique bf16 result)
         M, N, K = 2048, 1536, 2048
         a, b = oracle.exact_inputs(M, N, K, seed=7)
