@@ -46,15 +46,23 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// Kernel configurations: {K slabs per stage, N sub-tiles per pair tile}.
-enum Variant { kV256x64 = 0, kV256x128 = 1, kV512x64 = 2, kNumVariants = 3 };
-constexpr int kVariantSlabs[kNumVariants] = {1, 2, 1};
-constexpr int kVariantNSub[kNumVariants] = {1, 1, 2};
+// Kernel configurations, named pair-tile width x stage K: {K slabs per
+// stage, N sub-tiles per pair tile, sub-tile width}.
+enum Variant {
+  kV256x64 = 0, kV256x128 = 1, kV512x64 = 2, kV128x64 = 3, kV64x64 = 4, kNumVariants = 5
+};
+constexpr int kVariantSlabs[kNumVariants] = {1, 2, 1, 1, 1};
+constexpr int kVariantNSub[kNumVariants] = {1, 1, 2, 1, 1};
+constexpr int kVariantSubW[kNumVariants] = {256, 256, 256, 128, 64};
 
 template <int V>
 struct VariantCfg {
-  using C = Cfg<kVariantSlabs[V], kVariantNSub[V]>;
+  using C = Cfg<kVariantSlabs[V], kVariantNSub[V], kVariantSubW[V]>;
 };
+
+template <bool kProfile, int V, int kOut>
+constexpr auto pair_kernel =
+    gemm_bf16_pair_kernel<kProfile, kVariantSlabs[V], kVariantNSub[V], kOut, kVariantSubW[V]>;
 
 constexpr int kMaxDevices = 64;
 
@@ -62,7 +70,7 @@ struct DeviceState {
   bool ready = false;
   int init_status = B200_OK;
   int sms = 0;
-  int max_pairs[kNumVariants] = {0, 0, 0};  // co-resident 2-CTA clusters per variant
+  int max_pairs[kNumVariants] = {};         // co-resident 2-CTA clusters per variant
   int* status = nullptr;                    // device error word
   cudaMemPool_t pool = nullptr;             // stream-ordered split-K workspaces
   int sk_clusters[16][4] = {};              // skinny-cluster kernels: resident clusters of 1,2,4,8
@@ -102,7 +110,7 @@ int tuning_tile_n() {
   int v = g_tile_n.load();
   if (v < 0) {
     v = env_int("B200_GEMM_TILE_N", 0, 0, 512);
-    if (v != 256 && v != 512) v = 0;
+    if (v != 64 && v != 128 && v != 256 && v != 512) v = 0;
     g_tile_n.store(v);
   }
   return v;
@@ -141,9 +149,7 @@ int query_pairs(int sms, int* out) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(
-          &n, gemm_bf16_pair_kernel<false, kVariantSlabs[V], kVariantNSub[V], kOutBf16>, &cfg) !=
-      cudaSuccess)
+  if (cudaOccupancyMaxActiveClusters(&n, pair_kernel<false, V, kOutBf16>, &cfg) != cudaSuccess)
     return B200_ERR_LAUNCH;
   *out = n;
   return B200_OK;
@@ -151,15 +157,32 @@ int query_pairs(int sms, int* out) {
 
 template <bool kProfile, int V, int kOut>
 bool set_smem_limit() {
-  return cudaFuncSetAttribute(
-             gemm_bf16_pair_kernel<kProfile, kVariantSlabs[V], kVariantNSub[V], kOut>,
-             cudaFuncAttributeMaxDynamicSharedMemorySize, VariantCfg<V>::C::kSmemBytes) ==
-         cudaSuccess;
+  return cudaFuncSetAttribute(pair_kernel<kProfile, V, kOut>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              VariantCfg<V>::C::kSmemBytes) == cudaSuccess;
 }
 
 template <int V>
 bool set_smem_limits() {
   return set_smem_limit<false, V, kOutBf16>() && set_smem_limit<true, V, kOutBf16>();
+}
+
+// bf16-output limits (with and without the profiler) and resident pairs of
+// every configuration.
+int init_variants(int sms, int* max_pairs) {
+  if (!set_smem_limits<kV256x64>() || !set_smem_limits<kV256x128>() ||
+      !set_smem_limits<kV512x64>() || !set_smem_limits<kV128x64>() ||
+      !set_smem_limits<kV64x64>())
+    return B200_ERR_LAUNCH;
+  if (query_pairs<kV256x64>(sms, &max_pairs[kV256x64]) != B200_OK ||
+      query_pairs<kV256x128>(sms, &max_pairs[kV256x128]) != B200_OK ||
+      query_pairs<kV512x64>(sms, &max_pairs[kV512x64]) != B200_OK ||
+      query_pairs<kV128x64>(sms, &max_pairs[kV128x64]) != B200_OK ||
+      query_pairs<kV64x64>(sms, &max_pairs[kV64x64]) != B200_OK)
+    return B200_ERR_LAUNCH;
+  for (int v = 0; v < kNumVariants; ++v)
+    if (max_pairs[v] < 1) return B200_ERR_LAUNCH;
+  return B200_OK;
 }
 
 template <int kMp, int kSlabs>
@@ -234,17 +257,12 @@ int init_device(DeviceState& d, int dev) {
   if (prop.major != 10 || prop.minor != 0) return B200_ERR_UNSUPPORTED_DEVICE;  // sm_100a only
   if (encode_tiled() == nullptr) return B200_ERR_TENSOR_MAP;
   d.sms = prop.multiProcessorCount;
-  if (!set_smem_limits<kV256x64>() || !set_smem_limits<kV256x128>() ||
-      !set_smem_limits<kV512x64>() || !set_smem_limit<false, kV256x64, kOutF32>() ||
+  if (!set_smem_limit<false, kV256x64, kOutF32>() ||
       !set_smem_limit<false, kV256x64, kOutF32Add>() ||
       !set_smem_limit<false, kV256x64, kOutBf16Epi>() || !set_skinny_limits())
     return B200_ERR_LAUNCH;
-  if (query_pairs<kV256x64>(d.sms, &d.max_pairs[kV256x64]) != B200_OK ||
-      query_pairs<kV256x128>(d.sms, &d.max_pairs[kV256x128]) != B200_OK ||
-      query_pairs<kV512x64>(d.sms, &d.max_pairs[kV512x64]) != B200_OK)
-    return B200_ERR_LAUNCH;
-  for (int v = 0; v < kNumVariants; ++v)
-    if (d.max_pairs[v] < 1) return B200_ERR_LAUNCH;
+  const int vst = init_variants(d.sms, d.max_pairs);
+  if (vst != B200_OK) return vst;
   if (!skc_init_all(d)) return B200_ERR_LAUNCH;
   if (cudaMalloc(&d.status, sizeof(int)) != cudaSuccess ||
       cudaMemset(d.status, 0, sizeof(int)) != cudaSuccess)
@@ -293,18 +311,38 @@ double wave_efficiency(long long tiles, int pairs) {
 // Configuration for an M x N problem.  512-wide pair tiles read 25% fewer
 // operand bytes per FLOP through L2 (one A slab feeds two MMAs), which under
 // the 1 kW power cap turns into clock; they are chosen unless halving the
-// tile count costs wave efficiency or leaves pairs idle.
+// tile count costs wave efficiency or leaves pairs idle.  Grids of fewer
+// 256-wide tiles than pairs leave SMs idle while each pair walks the whole
+// K; 128- or 64-wide tiles then finish sooner: the width minimising
+// waves x width wins, the wider one on a tie.
 int choose_variant(int M, int N, const int* max_pairs) {
   const int tn = tuning_tile_n();
   if (tn == 512) return kV512x64;
+  if (tn == 128) return kV128x64;
+  if (tn == 64) return kV64x64;
   const int v256 = stage_slabs() == 2 ? kV256x128 : kV256x64;
   if (tn == 256) return v256;
-  const long long t256 = ceil_div(M, kPairM) * ceil_div(N, kSubN);
-  const long long t512 = ceil_div(M, kPairM) * ceil_div(N, 2 * kSubN);
-  const int p256 = max_pairs ? max_pairs[v256] : 74;
-  const int p512 = max_pairs ? max_pairs[kV512x64] : 74;
-  if (t512 < p512) return v256;
-  return wave_efficiency(t512, p512) + 0.02 >= wave_efficiency(t256, p256) ? kV512x64 : v256;
+  auto pairs = [&](int v) { return max_pairs ? max_pairs[v] : 74; };
+  const long long rows = ceil_div(M, kPairM);
+  const long long t256 = rows * ceil_div(N, kSubN);
+  const long long t512 = rows * ceil_div(N, 2 * kSubN);
+  if (t256 < pairs(v256)) {
+    int best = v256;
+    long long best_cost = kSubN;  // one wave
+    for (const int v : {kV128x64, kV64x64}) {
+      const long long t = rows * ceil_div(N, kVariantSubW[v]);
+      const long long cost = ceil_div(t, pairs(v)) * kVariantSubW[v];
+      if (cost < best_cost) {
+        best = v;
+        best_cost = cost;
+      }
+    }
+    return best;
+  }
+  if (t512 < pairs(kV512x64)) return v256;
+  return wave_efficiency(t512, pairs(kV512x64)) + 0.02 >= wave_efficiency(t256, pairs(v256))
+             ? kV512x64
+             : v256;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -351,18 +389,19 @@ int validate(const void* A, const void* B, void* C, int M, int N, int K, int lda
   return B200_OK;
 }
 
-// Slices for split-K.  A grid of fewer 256 x 256 tiles than half the pairs
-// leaves SMs idle (the skinny, HBM-bound shapes), so a deep K is cut into up
-// to 16 slices of at least 8 K-blocks.  Shallow problems (fewer than 32
-// K-blocks, e.g. 1024^3) are not split: the workspace clear and the rounding
-// pass cost more than the idle SMs.
-int choose_splits(long long tiles, int k_blocks, int pairs) {
+// Slices for split-K (units of 256 x 256 tiles x K slices; the fp32
+// workspace is cleared, reduce-added into and rounded: two extra passes).
+// It pays only when even 64-wide pair tiles would leave more than half the
+// pairs idle and K is deep: then K is cut into up to 16 slices of at least 8
+// K-blocks.  Shallow problems (fewer than 32 K-blocks) are never split.
+int choose_splits(int M, int N, int k_blocks, int pairs) {
   const int forced = tuning_splits();
   int s;
   if (forced > 0) {
     s = forced;
   } else {
-    if (tiles * 2 > pairs || k_blocks < 32) return 1;
+    const long long narrow = ceil_div(M, kPairM) * ceil_div(N, kVariantSubW[kV64x64]);
+    if (narrow * 2 > pairs || k_blocks < 32) return 1;
     s = k_blocks / 8;
     if (s > 16) s = 16;
   }
@@ -381,11 +420,31 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
   args.splits = (int)ceil_div(args.k_blocks, args.kb_per_split);  // every slice non-empty
   const long long units = (long long)args.tiles_m * args.tiles_n * args.splits;
   const int pairs = (int)(units < d.max_pairs[V] ? units : d.max_pairs[V]);
-  gemm_bf16_pair_kernel<kProfile, kVariantSlabs[V], kVariantNSub[V], kOut>
-      <<<2 * pairs, C::kThreads, C::kSmemBytes, stream>>>(ta, tb, tc, args);
+  pair_kernel<kProfile, V, kOut><<<2 * pairs, C::kThreads, C::kSmemBytes, stream>>>(ta, tb, tc,
+                                                                                   args);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
 }
 
+// bf16 GEMM with configuration v.  tb maps B with 128-row boxes (the
+// 256-wide sub-tiles); narrower sub-tiles load kSubW / 2 rows of B per CTA,
+// so their map is encoded here.
+template <bool kProfile>
+int launch_bf16(int v, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                const void* B, int ldb, const GemmArgs& args, const DeviceState& d,
+                cudaStream_t stream) {
+  if (v == kV128x64 || v == kV64x64) {
+    CUtensorMap tbn;
+    if (encode_2d(&tbn, B, args.K, args.N, ldb, kSlabK, kVariantSubW[v] / 2) != B200_OK)
+      return B200_ERR_TENSOR_MAP;
+    return v == kV128x64 ? launch<kProfile, kV128x64, kOutBf16>(ta, tbn, tc, args, 1, d, stream)
+                         : launch<kProfile, kV64x64, kOutBf16>(ta, tbn, tc, args, 1, d, stream);
+  }
+  switch (v) {
+    case kV256x128: return launch<kProfile, kV256x128, kOutBf16>(ta, tb, tc, args, 1, d, stream);
+    case kV512x64: return launch<kProfile, kV512x64, kOutBf16>(ta, tb, tc, args, 1, d, stream);
+    default: return launch<kProfile, kV256x64, kOutBf16>(ta, tb, tc, args, 1, d, stream);
+  }
+}
 
 int cast_to_bf16(const float* W, int ldw, void* C, int ldc, int M, int N, int sms,
                  cudaStream_t stream, const EpiArgs* epi = nullptr) {
@@ -588,6 +647,34 @@ bool use_skinny(int M, int N, int K) {
   return enabled && M <= kSkinnyMaxM && N >= 1024 && K >= 512;
 }
 
+// K slices a skinny call uses (for reporting): the cluster size of the
+// cluster kernel (M <= 16), else the persistent kernel's slice count.  Without
+// a device, 148 SMs are assumed and the persistent kernel is reported.
+int skinny_slices(int M, int N, int K, const DeviceState* d) {
+  static const int mode = env_int("B200_GEMM_SKINNY", 1, 0, 2);
+  const int forced = tuning_splits();
+  const long long tiles = ceil_div(N, 128);
+  if (d && (mode == 2 || M <= 16)) {
+    const int k_blocks = (int)ceil_div(K, kSlabK);
+    if (forced > 0) {
+      int ci = 0;
+      while (ci < 3 && (2 << ci) <= forced) ++ci;
+      return 1 << ci;
+    }
+    // the ring depth the default occupancy picks for this M (run_skinny_cluster)
+    const int I = M <= 16 ? 1 : M <= 32 ? 3 : M <= 64 ? 5 : M <= 128 ? 6 : 7;
+    for (int c = 3; c >= 1; --c) {
+      const long long clusters = d->sk_clusters[I][c];
+      if (clusters > 0 && tiles <= clusters && k_blocks >= 8 * (1 << c)) return 1 << c;
+    }
+    return 1;
+  }
+  const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  const int k_blocks = (int)ceil_div(K, skinny_fit_slabs(mp, skinny_slabs()) * kSlabK);
+  const int s = choose_skinny_splits(tiles, k_blocks, d ? d->sms : 148, M, N, K);
+  return (int)ceil_div(k_blocks, ceil_div(k_blocks, s));
+}
+
 GemmArgs base_args(int M, int N, int K, const DeviceState& d, long long* prof, int entries) {
   GemmArgs args;
   args.M = M;
@@ -637,8 +724,7 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda
   // Split-K (not with the profiler): tiles accumulate their K slices into a
   // zeroed fp32 workspace by TMA reduce-add, then one pass rounds to bf16.
   if (!kProfile) {
-    const long long tiles = ceil_div(M, kPairM) * ceil_div(N, kSubN);
-    const int splits = choose_splits(tiles, (int)ceil_div(K, kSlabK), d->max_pairs[kV256x64]);
+    const int splits = choose_splits(M, N, (int)ceil_div(K, kSlabK), d->max_pairs[kV256x64]);
     if (splits > 1) {
       const int ldw = (int)ceil_div(N, 8) * 8;
       const size_t bytes = (size_t)M * ldw * sizeof(float);
@@ -659,11 +745,8 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda
     }
   }
   if (!kProfile && epi) return launch<false, kV256x64, kOutBf16Epi>(ta, tb, tc, args, 1, *d, stream);
-  switch (choose_variant(M, N, d->max_pairs)) {
-    case kV256x128: return launch<kProfile, kV256x128, kOutBf16>(ta, tb, tc, args, 1, *d, stream);
-    case kV512x64: return launch<kProfile, kV512x64, kOutBf16>(ta, tb, tc, args, 1, *d, stream);
-    default: return launch<kProfile, kV256x64, kOutBf16>(ta, tb, tc, args, 1, *d, stream);
-  }
+  return launch_bf16<kProfile>(choose_variant(M, N, d->max_pairs), ta, tb, tc, B, ldb, args, *d,
+                               stream);
 }
 
 // fp32 C = A * B^T (no rounding), 256 x 256 tiles: the K-split partials.
@@ -854,6 +937,8 @@ int b200_gemm_launch_shape(int M, int N, int K, int* tiles, int* grid, int* smem
   int smem, thr;
   if (v == kV512x64) shape_of<kV512x64>(&tile_n, &smem, &thr);
   else if (v == kV256x128) shape_of<kV256x128>(&tile_n, &smem, &thr);
+  else if (v == kV128x64) shape_of<kV128x64>(&tile_n, &smem, &thr);
+  else if (v == kV64x64) shape_of<kV64x64>(&tile_n, &smem, &thr);
   else shape_of<kV256x64>(&tile_n, &smem, &thr);
   const long long t = ceil_div(M, kPairM) * ceil_div(N, tile_n);
   if (tiles) *tiles = (int)t;
@@ -891,7 +976,9 @@ int b200_gemm_device_status(int clear, int* status_out) {
 }
 
 int b200_gemm_set_tuning(int tile_n, int stage_slabs, int raster_group) {
-  if ((tile_n != 0 && tile_n != -1 && tile_n != 256 && tile_n != 512) || stage_slabs < 0 ||
+  if ((tile_n != 0 && tile_n != -1 && tile_n != 64 && tile_n != 128 && tile_n != 256 &&
+       tile_n != 512) ||
+      stage_slabs < 0 ||
       stage_slabs > 2)
     return B200_ERR_INVALID_ARGUMENT;
   if (tile_n == -1) g_tile_n.store(0);
@@ -910,11 +997,10 @@ int b200_gemm_set_splits(int splits) {
 int b200_gemm_get_splits(int M, int N, int K, int* splits) {
   if (!splits || M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARGUMENT;
   DeviceState* d = nullptr;
-  const int pairs = device_state(&d) == B200_OK ? d->max_pairs[kV256x64] : 74;
-  *splits = (M == 0 || N == 0 || K == 0)
-                ? 1
-                : choose_splits(ceil_div(M, kPairM) * ceil_div(N, kSubN),
-                                (int)ceil_div(K, kSlabK), pairs);
+  const bool have_dev = device_state(&d) == B200_OK;
+  if (M == 0 || N == 0 || K == 0) *splits = 1;
+  else if (use_skinny(M, N, K)) *splits = skinny_slices(M, N, K, have_dev ? d : nullptr);
+  else *splits = choose_splits(M, N, (int)ceil_div(K, kSlabK), have_dev ? d->max_pairs[kV256x64] : 74);
   return B200_OK;
 }
 
@@ -1111,15 +1197,9 @@ int noalloc_setup(NoAllocDevice& nd, int dev) {
   if (prop.major != 10 || prop.minor != 0) return B200_ERR_UNSUPPORTED_DEVICE;
   if (encode_tiled() == nullptr) return B200_ERR_TENSOR_MAP;
   nd.launch.sms = prop.multiProcessorCount;
-  if (!set_smem_limits<kV256x64>() || !set_smem_limits<kV256x128>() ||
-      !set_smem_limits<kV512x64>() || !set_smem_limit<false, kV256x64, kOutF32Add>())
-    return B200_ERR_LAUNCH;
-  if (query_pairs<kV256x64>(nd.launch.sms, &nd.launch.max_pairs[kV256x64]) != B200_OK ||
-      query_pairs<kV256x128>(nd.launch.sms, &nd.launch.max_pairs[kV256x128]) != B200_OK ||
-      query_pairs<kV512x64>(nd.launch.sms, &nd.launch.max_pairs[kV512x64]) != B200_OK)
-    return B200_ERR_LAUNCH;
-  for (int v = 0; v < kNumVariants; ++v)
-    if (nd.launch.max_pairs[v] < 1) return B200_ERR_LAUNCH;
+  if (!set_smem_limit<false, kV256x64, kOutF32Add>()) return B200_ERR_LAUNCH;
+  const int vst = init_variants(nd.launch.sms, nd.launch.max_pairs);
+  if (vst != B200_OK) return vst;
   // In host code g_noalloc_scratch names a host-side stand-in; the kernel
   // must be given the device address.
   void* p = nullptr;
@@ -1160,9 +1240,8 @@ int run_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K,
     return cudaMemset2DAsync(C, (size_t)ldc * 2, 0, (size_t)N * 2, M, stream) == cudaSuccess
                ? B200_OK
                : B200_ERR_LAUNCH;
-  const long long tiles = ceil_div(M, kPairM) * ceil_div(N, kSubN);
   const int splits =
-      choose_splits(tiles, (int)ceil_div(K, kSlabK), nd->launch.max_pairs[kV256x64]);
+      choose_splits(M, N, (int)ceil_div(K, kSlabK), nd->launch.max_pairs[kV256x64]);
   const int ldw = (int)ceil_div(N, 8) * 8;
   const size_t ws_bytes = (size_t)M * ldw * sizeof(float);
   if (splits > 1 && ws_bytes > kNoAllocWorkspaceBytes) return B200_ERR_TOO_LARGE;
@@ -1186,14 +1265,8 @@ int run_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K,
     return cast_to_bf16(W, ldw, C, ldc, M, N, nd->launch.sms, stream);
   }
   if (encode_2d(&tc, C, N, M, ldc, kStoreCols, 32) != B200_OK) return B200_ERR_TENSOR_MAP;
-  switch (choose_variant(M, N, nd->launch.max_pairs)) {
-    case kV256x128:
-      return launch<false, kV256x128, kOutBf16>(ta, tb, tc, args, 1, nd->launch, stream);
-    case kV512x64:
-      return launch<false, kV512x64, kOutBf16>(ta, tb, tc, args, 1, nd->launch, stream);
-    default:
-      return launch<false, kV256x64, kOutBf16>(ta, tb, tc, args, 1, nd->launch, stream);
-  }
+  return launch_bf16<false>(choose_variant(M, N, nd->launch.max_pairs), ta, tb, tc, B, ldb, args,
+                            nd->launch, stream);
 }
 
 }  // namespace

@@ -331,15 +331,16 @@ __device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <bool kProfile, int kSlabs, int kNSub, int kOut>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<kSlabs, kNSub>::kThreads, 1)
+template <bool kProfile, int kSlabs, int kNSub, int kOut, int kSubW = kSubN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<kSlabs, kNSub, kSubW>::kThreads, 1)
 gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_c,
                       const GemmArgs args) {
-  using P = Cfg<kSlabs, kNSub>;
+  using P = Cfg<kSlabs, kNSub, kSubW>;
   static_assert(kOut == kOutBf16 || kOut == kOutKsplit || kNSub == 1,
                 "fp32 outputs and fused epilogues use 256-wide pair tiles");
+  static_assert(kSubW == kSubN || kOut == kOutBf16, "narrow sub-tiles: plain bf16 output only");
   constexpr int kStages = P::kStages;
   constexpr int kAccBufs = P::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
@@ -418,7 +419,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
         int tm, tn, kb0, kb1;
         unit_coord<kOut>(u, args, &tm, &tn, &kb0, &kb1);
         const int a_row = tm * kPairM + (int)rank * kCtaM;
-        const int b_row = tn * P::kTileN + (int)rank * kCtaN;
+        const int b_row = tn * P::kTileN + (int)rank * P::kRowsB;
         for (int kb = kb0; kb < kb1; ++kb) {
           if constexpr (kProfile) prof.start(kTagWaitMMA);
           if (!wait_bounded(smem_u32(&bar_empty[stage]), phase ^ 1u, wctx, kErrWaitEmpty)) {
@@ -440,8 +441,8 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
             tma_load_2d_pair(sa + sl * kSlabBytes, &tmap_a, x, a_row, fb);
 #pragma unroll
             for (int sub = 0; sub < kNSub; ++sub)
-              tma_load_2d_pair(sa + P::kBytesA + (sub * kSlabs + sl) * kSlabBytes, &tmap_b, x,
-                               b_row + sub * kSubN, fb);
+              tma_load_2d_pair(sa + P::kBytesA + (sub * kSlabs + sl) * P::kSlabB, &tmap_b, x,
+                               b_row + sub * kSubW, fb);
           }
           if constexpr (kProfile) prof.stop();
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
@@ -453,7 +454,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     if (rank == 0 && lane == 0) {
-      const uint32_t idesc = make_idesc_bf16_f32(kPairM, kSubN);
+      const uint32_t idesc = make_idesc_bf16_f32(kPairM, kSubW);
       const uint32_t empty_self = cluster_map(smem_u32(&bar_empty[0]), 0);
       const uint32_t accf_self = cluster_map(smem_u32(&bar_acc_full[0]), 0);
       const uint32_t accf_peer = cluster_map(smem_u32(&bar_acc_full[0]), 1);
@@ -487,9 +488,9 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
 #pragma unroll
               for (int sub = 0; sub < kNSub; ++sub) {
                 const uint64_t bdesc =
-                    make_sdesc_k128(sa + P::kBytesA + (sub * kSlabs + sl) * kSlabBytes);
+                    make_sdesc_k128(sa + P::kBytesA + (sub * kSlabs + sl) * P::kSlabB);
                 // +32 B per K16 step inside the 128 B swizzled row (>>4 => +2)
-                umma_bf16_pair(d_tmem + sub * kSubN, adesc + 2ull * k, bdesc + 2ull * k, idesc,
+                umma_bf16_pair(d_tmem + sub * kSubW, adesc + 2ull * k, bdesc + 2ull * k, idesc,
                                (kb != kb0 || sl != 0 || k != 0) ? 1u : 0u);
               }
             }
@@ -540,9 +541,9 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
         if (lane == 0) { prof.stop(); prof.start(kTagEpilogue); }
       }
       const uint32_t tbase =
-          tmem_base + buf * P::kTileN + sub * kSubN + ((uint32_t)(quarter * 32) << 16);
+          tmem_base + buf * P::kTileN + sub * kSubW + ((uint32_t)(quarter * 32) << 16);
       const int row0 = tm * kPairM + (int)rank * kCtaM + quarter * 32;
-      const int col0 = tn * P::kTileN + sub * kSubN;
+      const int col0 = tn * P::kTileN + sub * kSubW;
       // Row `lane` of a 32x64 box is 8 chunks of 16 B; chunk j is stored at
       // position j ^ (row % 8) -- the TMA 128 B swizzle pattern.
       const uint32_t row_off = lane * 128u;
@@ -609,7 +610,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           out_row = row0 - ks.rank * ks.tiles_m_own * kPairM;
         }
 #pragma unroll 1
-        for (int c = 0; c < kSubN / kStoreCols; ++c) {
+        for (int c = 0; c < kSubW / kStoreCols; ++c) {
           uint32_t v0[32], v1[32];
           tmem_ld_32x32b_x32(tbase + c * kStoreCols, v0);
           tmem_ld_32x32b_x32(tbase + c * kStoreCols + 32, v1);
@@ -622,7 +623,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
             ks_accumulate(v0, recv, recv_stride, 2 * c, args.ks.rank, args.ks.nranks);
             ks_accumulate(v1, recv, recv_stride, 2 * c + 1, args.ks.rank, args.ks.nranks);
           }
-          if (c == kSubN / kStoreCols - 1) {
+          if (c == kSubW / kStoreCols - 1) {
             // All of this warp's part of the buffer is in registers: hand
             // TMEM back to the MMA.
             tc_fence_before_sync();

@@ -47,7 +47,10 @@ enum OutMode : int {
 
 // Kernel configuration.
 //   kSlabs  K slabs of 64 per pipeline stage (stage K = 64 * kSlabs)
-//   kNSub   256-wide N sub-tiles per pair tile: 1 -> 256 x 256 pair tiles with
+//   kSubW   width of one N sub-tile (= MMA N): 256, or 128 / 64 for grids too
+//           small to occupy every SM with 256-wide tiles (kNSub = 1 only);
+//           each CTA loads kSubW / 2 rows of B per sub-tile
+//   kNSub   N sub-tiles per pair tile: 1 -> 256 x kSubW pair tiles with
 //           two TMEM accumulators (epilogue of tile i overlaps the MMAs of
 //           tile i+1); 2 -> 256 x 512 pair tiles with one 512-column
 //           accumulator, where each A slab feeds two MMAs, so 25% fewer
@@ -56,16 +59,20 @@ enum OutMode : int {
 // A stage holds kSlabs slabs of A, then kNSub x kSlabs slabs of B (16 KiB
 // each, 1 KiB aligned); the ring depth is whatever fits beside the epilogue
 // staging buffers.
-template <int kSlabs, int kNSub>
+template <int kSlabs, int kNSub, int kSubW = kSubN>
 struct Cfg {
-  static constexpr int kTileN = kNSub * kSubN;
+  static_assert(kSubW == 256 || (kNSub == 1 && (kSubW == 128 || kSubW == 64)),
+                "sub-tiles are 256 wide, or 128 / 64 wide in single-sub-tile configurations");
+  static constexpr int kRowsB = kSubW / 2;              // rows of B per CTA per sub-tile
+  static constexpr int kSlabB = kRowsB * kSlabK * 2;    // bytes of one B slab (1 KiB multiple)
+  static constexpr int kTileN = kNSub * kSubW;
   static constexpr int kAccBufs = kNSub == 1 ? 2 : 1;
   static constexpr int kEpiWarps = 4 * kNSub;          // one per (lane quarter, sub-tile)
   static constexpr int kWarps = 2 + kEpiWarps;         // producer, MMA, epilogue
   static constexpr int kThreads = 32 * kWarps;
   static constexpr int kBK = kSlabs * kSlabK;
   static constexpr int kBytesA = kSlabs * kSlabBytes;
-  static constexpr int kBytesB = kNSub * kSlabs * kSlabBytes;
+  static constexpr int kBytesB = kNSub * kSlabs * kSlabB;
   static constexpr int kStageBytes = kBytesA + kBytesB;
   // 256-wide tiles: two staging buffers per epilogue warp, so storing chunk
   // c overlaps converting chunk c+1.  512-wide tiles: the epilogue first

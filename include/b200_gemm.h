@@ -101,7 +101,9 @@ int b200_gemm_device_status(int clear, int* status_out);
 /* Process-wide tuning.
  *   tile_n        pair-tile width: 256 (two TMEM accumulators, epilogue
  *                 overlapped), 512 (one A slab feeds two MMAs: 25% fewer
- *                 operand bytes per FLOP) or -1 to choose per shape; 0 keeps
+ *                 operand bytes per FLOP), 128 or 64 (more, shorter tiles
+ *                 for grids that leave SMs idle) or -1 to choose per shape;
+ *                 0 keeps
  *   stage_slabs   K slabs of 64 per stage for 256-wide tiles (1: 6 stages of
  *                 K=64, 2: 3 stages of K=128); 0 keeps
  *   raster_group  band width, in tiles, of the persistent raster (positive:

@@ -60,7 +60,8 @@ def within_tol(C, R, A, Bt, rows=None):
     return m
 
 
-CONFIGS = {"n256_bk64": (256, 1), "n256_bk128": (256, 2), "n512_bk64": (512, 1)}
+CONFIGS = {"n256_bk64": (256, 1), "n256_bk128": (256, 2), "n512_bk64": (512, 1),
+           "n128_bk64": (128, 1), "n64_bk64": (64, 1)}
 
 
 @pytest.fixture(autouse=True, params=list(CONFIGS), ids=list(CONFIGS))

@@ -120,5 +120,16 @@ def test_launch_shape_without_gpu():
         assert capi.launch_shape(8192, 8192, 8192)["threads"] == 320
         assert capi.launch_shape(2048, 2048, 2048)["threads"] == 192
         assert capi.launch_shape(16, 8192, 8192)["threads"] == 192
+        # grids under one wave of 256-wide tiles: the width minimising
+        # waves x width (no device: 74 pairs assumed)
+        assert capi.launch_shape(1024, 1024, 1024)["tiles"] == 4 * 16      # 64 wide
+        assert capi.launch_shape(768, 1024, 1024)["tiles"] == 3 * 16       # 64 wide
+        assert capi.launch_shape(1024, 2048, 1024)["tiles"] == 4 * 16      # 128 wide
+        assert capi.launch_shape(2048, 2048, 2048)["tiles"] == 8 * 8       # ties keep 256
+        for width, tiles in ((128, 32 * 64), (64, 32 * 128)):
+            capi.set_tuning(width, 1, 0)
+            s = capi.launch_shape(8192, 8192, 8192)
+            assert s["tiles"] == tiles and s["threads"] == 192
+            assert s["smem_bytes"] <= 227 * 1024
     finally:
         capi.set_tuning(before["tile_n"] or -1, before["stage_slabs"], before["raster_group"])

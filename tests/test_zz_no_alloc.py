@@ -12,7 +12,8 @@ from blackwell_gemm_b200 import capi, parity, workloads
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(16, 8192, 8192),      # skinny: split-K through the fixed workspace
+SHAPES = [(256, 2048, 8192),     # split-K through the fixed workspace
+          (16, 8192, 8192),      # skinny
           (1024, 1024, 1024),    # not split: only the error word is used
           (300, 520, 4096)]      # ragged
 
