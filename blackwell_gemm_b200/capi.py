@@ -30,6 +30,7 @@ DEVICE_WAIT_CODES = {
     0x1005: "final MMA drain",
     0x1006: "wait probe",
     0x1007: "K-split: a peer's piece of an own tile never arrived",
+    0x1008: "stream-K: an earlier CTA's partial tile never arrived",
 }
 
 KSPLIT_HANDLE_BYTES = 128
@@ -47,6 +48,7 @@ SIGNATURES = {
     "b200_gemm_bf16_epilogue": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, ctypes.c_float, _vp,
                                      ctypes.c_float, _vp, _i, _vp]),
     "b200_gemm_set_splits": (_i, [_i]),
+    "b200_gemm_set_skinny_mode": (_i, [_i]),
     "b200_gemm_get_splits": (_i, [_i, _i, _i, _ip]),
     "b200_gemm_profile_rows": (_i, [_i, _i, _i, _ip]),
     "b200_gemm_device_status": (_i, [_i, _ip]),
@@ -132,6 +134,11 @@ def gemm_bf16_noalloc(a_ptr: int, b_ptr: int, c_ptr: int, M: int, N: int, K: int
 
 def set_splits(splits: int) -> None:
     check(lib().b200_gemm_set_splits(int(splits)), "set_splits")
+
+
+def set_skinny_mode(mode: int) -> None:
+    """0 off, 1 per shape (default), 2 cluster kernel, 3 stream-K kernel."""
+    check(lib().b200_gemm_set_skinny_mode(mode), "b200_gemm_set_skinny_mode")
 
 
 def get_splits(M: int, N: int, K: int) -> int:

@@ -95,6 +95,26 @@ std::atomic<int> g_tile_n{-1};
 std::atomic<int> g_slabs{-1};
 std::atomic<int> g_group{0};
 std::atomic<int> g_splits{-1};
+std::atomic<int> g_skinny{-1};
+
+// L2 cache hints of the skinny kernels' loads (B200_GEMM_L2_HINT, default 1):
+// B, read once, evict-first; A, read by every CTA, evict-last.
+int skinny_l2_hint() {
+  static const int h = env_int("B200_GEMM_L2_HINT", 1, 0, 1);
+  return h;
+}
+
+// Skinny-M path (M <= 256): 0 = off, 1 = chosen per shape, 2 = the cluster
+// kernel for every M, 3 = the stream-K kernel for every M.  Initialised from
+// B200_GEMM_SKINNY, changeable through b200_gemm_set_skinny_mode.
+int skinny_mode() {
+  int v = g_skinny.load();
+  if (v < 0) {
+    v = env_int("B200_GEMM_SKINNY", 1, 0, 3);
+    g_skinny.store(v);
+  }
+  return v;
+}
 
 // Split-K slices: 0 = chosen per shape, 1 = never split, n = n slices.
 int tuning_splits() {
@@ -188,6 +208,9 @@ int init_variants(int sms, int* max_pairs) {
 template <int kMp, int kSlabs>
 bool set_skinny_limit() {
   return cudaFuncSetAttribute(gemm_skinny_kernel<kMp, kSlabs>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              SkinnyCfg<kMp, kSlabs>::kSmemBytes) == cudaSuccess &&
+         cudaFuncSetAttribute(gemm_skinny_stream_kernel<kMp, kSlabs>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                               SkinnyCfg<kMp, kSlabs>::kSmemBytes) == cudaSuccess;
 }
@@ -491,6 +514,7 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
       encode_2d(&ta, A, K, M, lda, kSlabK, kMp) != B200_OK)
     return B200_ERR_TENSOR_MAP;
   SkinnyArgs args;
+  args.l2_hint = skinny_l2_hint();
   args.M = M;
   args.N = N;
   args.K = K;
@@ -521,6 +545,74 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
   if (st == B200_OK) st = cast_to_bf16(W, ldw, C, ldc, M, N, d.sms, stream, epi);
   cudaFreeAsync(W, stream);
   return st;
+}
+
+// Stream-K skinny kernel (gemm_skinny_stream_kernel): G = min(SMs, work
+// items) CTAs, equal contiguous ranges of (tile, K block) items; partial
+// tiles meet in a per-call slot workspace whose flags are cleared first.
+long long stream_owner_host(long long x, long long total, int G) {
+  return ((x + 1) * G + total - 1) / total - 1;
+}
+
+template <int kMp, int kSlabs>
+int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                         int ldb, int ldc, DeviceState& d, cudaStream_t stream) {
+  using P = SkinnyCfg<kMp, kSlabs>;
+  CUtensorMap tb, ta, tc;
+  if (encode_2d(&tb, B, K, N, ldb, kSlabK, P::kRowsB) != B200_OK ||
+      encode_2d(&ta, A, K, M, lda, kSlabK, kMp) != B200_OK ||
+      encode_2d(&tc, C, N, M, ldc, 32, P::kChunk, false, false) != B200_OK)
+    return B200_ERR_TENSOR_MAP;
+  SkinnyStreamArgs args;
+  args.l2_hint = skinny_l2_hint();
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.tiles = (int)ceil_div(N, P::kRowsB);
+  args.k_blocks = (int)ceil_div(K, P::kBK);
+  args.total = (long long)args.tiles * args.k_blocks;
+  const int G = (int)(args.total < d.sms ? args.total : d.sms);
+  int max_seg = 1;
+  for (int t = 0; t < args.tiles; ++t) {
+    const long long x0 = (long long)t * args.k_blocks;
+    const long long segs = stream_owner_host(x0 + args.k_blocks - 1, args.total, G) -
+                           stream_owner_host(x0, args.total, G) + 1;
+    if (segs > max_seg) max_seg = (int)segs;
+  }
+  args.max_seg = max_seg;
+  args.status = d.status;
+  args.timeout_ns = g_timeout_ns.load();
+  const size_t flag_bytes = (size_t)ceil_div((long long)args.tiles * max_seg * 4 * 4, 256) * 256;
+  const size_t slot_bytes = (size_t)args.tiles * max_seg * kMp * P::kRowsB * sizeof(float);
+  char* ws = nullptr;
+  if (cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), flag_bytes + slot_bytes, d.pool,
+                              stream) != cudaSuccess) {
+    cudaGetLastError();
+    return B200_ERR_LAUNCH;
+  }
+  args.flags = reinterpret_cast<unsigned int*>(ws);
+  args.slots = reinterpret_cast<float*>(ws + flag_bytes);
+  int st = cudaMemsetAsync(ws, 0, flag_bytes, stream) == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
+  if (st == B200_OK) {
+    gemm_skinny_stream_kernel<kMp, kSlabs><<<G, P::kThreads, P::kSmemBytes, stream>>>(tb, ta, tc,
+                                                                                    args);
+    if (cudaGetLastError() != cudaSuccess) st = B200_ERR_LAUNCH;
+  }
+  cudaFreeAsync(ws, stream);
+  return st;
+}
+
+template <int kSlabs>
+int run_skinny_stream_slabs(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                            int ldb, int ldc, DeviceState& d, cudaStream_t stream) {
+#define B200_SKS(MP) \
+  launch_skinny_stream<MP, skinny_fit_slabs(MP, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d, stream)
+  if (M <= 16) return B200_SKS(16);
+  if (M <= 32) return B200_SKS(32);
+  if (M <= 64) return B200_SKS(64);
+  if (M <= 128) return B200_SKS(128);
+  return B200_SKS(256);
+#undef B200_SKS
 }
 
 template <int kSlabs>
@@ -576,6 +668,7 @@ int launch_skinny_cluster(const void* A, const void* B, void* C, int M, int N, i
       encode_2d(&ta, A, K, M, lda, kSlabK, S::kMp) != B200_OK)
     return B200_ERR_TENSOR_MAP;
   SkinnyClusterArgs args;
+  args.l2_hint = skinny_l2_hint();
   args.M = M;
   args.N = N;
   args.K = K;
@@ -627,8 +720,16 @@ int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int l
                int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi = nullptr) {
   // Up to 16 rows of A the single-launch cluster kernel is faster (no
   // workspace clear or rounding pass); above, the persistent kernel streams
-  // better.  B200_GEMM_SKINNY=2 forces the cluster kernel for every M.
-  static const int mode = env_int("B200_GEMM_SKINNY", 1, 0, 2);
+  // better.  B200_GEMM_SKINNY=2 forces the cluster kernel for every M,
+  // 3 the stream-K kernel.
+  const int mode = skinny_mode();
+  if (epi == nullptr && mode == 3) {
+    switch (skinny_slabs()) {
+      case 1: return run_skinny_stream_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
+      case 4: return run_skinny_stream_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
+      default: return run_skinny_stream_slabs<2>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
+    }
+  }
   // (The cluster kernel writes C directly, so fused epilogues take the
   // workspace kernel, whose rounding pass applies them.)
   if (epi == nullptr && (mode == 2 || M <= 16))
@@ -643,15 +744,14 @@ int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int l
 // Skinny path for M <= 256 when B is large enough to need every SM and K
 // deep enough to be worth streaming (B200_GEMM_SKINNY=0 disables it).
 bool use_skinny(int M, int N, int K) {
-  static const int enabled = env_int("B200_GEMM_SKINNY", 1, 0, 2);
-  return enabled && M <= kSkinnyMaxM && N >= 1024 && K >= 512;
+  return skinny_mode() != 0 && M <= kSkinnyMaxM && N >= 1024 && K >= 512;
 }
 
 // K slices a skinny call uses (for reporting): the cluster size of the
 // cluster kernel (M <= 16), else the persistent kernel's slice count.  Without
 // a device, 148 SMs are assumed and the persistent kernel is reported.
 int skinny_slices(int M, int N, int K, const DeviceState* d) {
-  static const int mode = env_int("B200_GEMM_SKINNY", 1, 0, 2);
+  const int mode = skinny_mode();
   const int forced = tuning_splits();
   const long long tiles = ceil_div(N, 128);
   if (d && (mode == 2 || M <= 16)) {
@@ -985,6 +1085,12 @@ int b200_gemm_set_tuning(int tile_n, int stage_slabs, int raster_group) {
   else if (tile_n != 0) g_tile_n.store(tile_n);
   if (stage_slabs > 0) g_slabs.store(stage_slabs);
   if (raster_group != 0) g_group.store(raster_group);
+  return B200_OK;
+}
+
+int b200_gemm_set_skinny_mode(int mode) {
+  if (mode < 0 || mode > 3) return B200_ERR_INVALID_ARGUMENT;
+  g_skinny.store(mode);
   return B200_OK;
 }
 

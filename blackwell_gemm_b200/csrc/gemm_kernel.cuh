@@ -69,6 +69,7 @@ enum : int {
   kErrWaitDrain = 0x1005,     // final wait for outstanding MMAs
   kErrWaitProbe = 0x1006,     // self-test kernel (wait that nothing releases)
   kErrWaitPeer = 0x1007,      // K-split: a peer's piece of an own tile never arrived
+  kErrWaitPartial = 0x1008,   // stream-K: an earlier CTA's partial tile never arrived
 };
 
 // Intra-kernel profiler tags; numbering and row format follow the

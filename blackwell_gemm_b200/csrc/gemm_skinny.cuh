@@ -23,6 +23,17 @@
 
 namespace b200 {
 
+// Every CTA reads the same rows of A.  Units that walk their K blocks in
+// the same order ask L2 for the same A slab at the same moment; starting
+// tile t's walk at an offset spreads those reads over t-dependent slabs.
+// K block number i (0 <= i < len) of a unit of tile t out of T:
+__device__ __forceinline__ int skinny_kb(int kb0, int len, int i, int t, int T) {
+  const int rot = (int)(((long long)t * len) / T) % len;
+  int j = i + rot;
+  if (j >= len) j -= len;
+  return kb0 + j;
+}
+
 template <int kMp, int kSlabs>
 struct SkinnyCfg {
   static_assert(kMp % 16 == 0 && kMp >= 16 && kMp <= 256, "MMA N must be 16..256, step 16");
@@ -57,6 +68,7 @@ constexpr int skinny_fit_slabs(int mp, int want) {
 
 struct SkinnyArgs {
   int M, N, K;
+  int l2_hint;       // 1: B loads evict-first, A loads evict-last in L2
   int tiles;         // ceil(N / 128)
   int k_blocks;      // ceil(K / kBK)
   int splits;        // K slices per tile
@@ -129,12 +141,15 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
 
   if (warp == 0) {
     if (lane == 0) {
+      const uint64_t pol_b = args.l2_hint ? l2_policy_evict_first() : l2_policy_evict_normal();
+      const uint64_t pol_a = args.l2_hint ? l2_policy_evict_last() : l2_policy_evict_normal();
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
         int tile, kb0, kb1;
         unit_range(u, &tile, &kb0, &kb1);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int i = 0; i < kb1 - kb0; ++i) {
+          const int kb = skinny_kb(kb0, kb1 - kb0, i, tile, args.tiles);
           if (!wait_bounded(smem_u32(&bar_empty[stage]), phase ^ 1u, wctx, kErrWaitEmpty)) {
             ok = false;
             break;
@@ -146,12 +161,12 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
           // segments are requested together.
 #pragma unroll
           for (int sl = 0; sl < kSlabs; ++sl)
-            tma_load_2d(sb + sl * P::kSlabB, &tmap_b, kb * P::kBK + sl * kSlabK,
-                        tile * P::kRowsB, fb);
+            tma_load_2d_hint(sb + sl * P::kSlabB, &tmap_b, kb * P::kBK + sl * kSlabK,
+                             tile * P::kRowsB, fb, pol_b);
 #pragma unroll
           for (int sl = 0; sl < kSlabs; ++sl)
-            tma_load_2d(sb + P::kBytesB + sl * P::kSlabA, &tmap_a, kb * P::kBK + sl * kSlabK, 0,
-                        fb);
+            tma_load_2d_hint(sb + P::kBytesB + sl * P::kSlabA, &tmap_a, kb * P::kBK + sl * kSlabK,
+                             0, fb, pol_a);
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
       }
@@ -171,7 +186,7 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
           break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + buf * kMp;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {  // slabs arrive in the producer's order
           if (!wait_bounded(smem_u32(&bar_full[stage]), phase, wctx, kErrWaitFull)) {
             ok = false;
             break;
@@ -287,6 +302,7 @@ struct SkinnyClusterCfg {
 
 struct SkinnyClusterArgs {
   int M, N, K;
+  int l2_hint;
   int k_blocks;       // ceil(K / 64)
   int kb_per;         // K blocks per cluster rank
   int ldc;            // C row stride (elements)
@@ -348,13 +364,17 @@ gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x 
   if (warp == 0) {
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
-      for (int kb = kb0; kb < kb1; ++kb) {
+      const uint64_t pol_b = args.l2_hint ? l2_policy_evict_first() : l2_policy_evict_normal();
+      const uint64_t pol_a = args.l2_hint ? l2_policy_evict_last() : l2_policy_evict_normal();
+      const int tiles = (int)(gridDim.x / csize);
+      for (int i = 0; i < kb1 - kb0; ++i) {
+        const int kb = skinny_kb(kb0, kb1 - kb0, i, tile, tiles);
         if (!wait_bounded(smem_u32(&bar_empty[stage]), phase ^ 1u, wctx, kErrWaitEmpty)) break;
         const uint32_t sb = smem_base + stage * P::kStageBytes;
         const uint32_t fb = smem_u32(&bar_full[stage]);
         mbar_arrive_expect_tx(fb, P::kStageBytes);
-        tma_load_2d(sb, &tmap_b, kb * kSlabK, tile * P::kRowsB, fb);
-        tma_load_2d(sb + P::kSlabB, &tmap_a, kb * kSlabK, 0, fb);
+        tma_load_2d_hint(sb, &tmap_b, kb * kSlabK, tile * P::kRowsB, fb, pol_b);
+        tma_load_2d_hint(sb + P::kSlabB, &tmap_a, kb * kSlabK, 0, fb, pol_a);
         if (++stage == kStages) { stage = 0; phase ^= 1u; }
       }
     }
@@ -427,6 +447,327 @@ gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x 
     }
     cluster_sync_all();
   }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc_1(tmem_base, P::kTmemAlloc);
+  }
+}
+
+}  // namespace b200
+
+namespace b200 {
+
+// ---------------------------------------------------------------------------
+// Stream-K variant: every SM streams the same number of B bytes, in one
+// launch, with no workspace clear of the output and no rounding pass.  The
+// problem's work items, (128-row block of B = tile) x (K block), are laid
+// out tile by tile and cut into G contiguous ranges of equal length, one per
+// CTA (G = SMs).  A range is the tail of one tile, whole tiles, then the
+// head of another:
+//   * a whole tile: the epilogue rounds TMEM to bf16 and TMA-stores C^T;
+//   * part of a tile: the epilogue writes the fp32 partial into slot j of
+//     the tile (j = this CTA's position among the tile's contributors, in K
+//     order) and raises flag (tile, j, lane quarter);
+//   * the CTA holding a tile's last K blocks (the tile is the first of its
+//     range) also finishes that tile after its range: it waits, bounded, for
+//     the earlier contributors' flags -- raised at the ends of their ranges --
+//     adds slots 0..j in K order, rounds and stores C.
+// Waits only point to CTAs of lower index, which the hardware dispatches
+// first.  Slots and flags live in a per-call workspace; the flags start at 0.
+struct SkinnyStreamArgs {
+  int M, N, K;
+  int l2_hint;
+  int tiles;         // ceil(N / 128)
+  int k_blocks;      // K blocks per tile, ceil(K / kBK)
+  long long total;   // tiles x k_blocks
+  int max_seg;       // slots per tile
+  float* slots;      // [tiles][max_seg][kMp][128] fp32
+  unsigned int* flags;  // [tiles][max_seg][4]
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ unsigned int ld_acquire_gpu_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_gpu_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// First CTA (of G) whose range [c total / G, (c+1) total / G) holds item x.
+__device__ __forceinline__ int stream_owner(long long x, long long total, int G) {
+  return (int)(((x + 1) * G + total - 1) / total) - 1;
+}
+
+template <int kMp, int kSlabs>
+__global__ void __launch_bounds__(192, 1)
+gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 64 x 128
+                          const __grid_constant__ CUtensorMap tmap_a,   // M x K, box 64 x Mp
+                          const __grid_constant__ CUtensorMap tmap_c,   // C bf16 M x N, box 32 x kChunk
+                          const SkinnyStreamArgs args) {
+  using P = SkinnyCfg<kMp, kSlabs>;
+  constexpr int kStages = P::kStages;
+  constexpr int kChunk = P::kChunk;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ alignas(8) uint64_t bar_full[kStages];
+  __shared__ alignas(8) uint64_t bar_empty[kStages];
+  __shared__ alignas(8) uint64_t bar_acc_full[2];
+  __shared__ alignas(8) uint64_t bar_acc_empty[2];
+  __shared__ alignas(8) uint64_t bar_drain;
+  __shared__ uint32_t tmem_slot;
+  __shared__ uint32_t abort_word;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const long long lo = (long long)blockIdx.x * args.total / G;
+  const long long hi = (long long)(blockIdx.x + 1) * args.total / G;
+  const int KB = args.k_blocks;
+  const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t store_base = smem_base + kStages * P::kStageBytes;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&bar_full[s]), 1);
+      mbar_init(smem_u32(&bar_empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&bar_acc_full[b]), 1);
+      mbar_init(smem_u32(&bar_acc_empty[b]), 4);
+    }
+    mbar_init(smem_u32(&bar_drain), 1);
+    abort_word = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_c);
+  }
+  if (warp == 1) {
+    tmem_alloc_1(smem_u32(&tmem_slot), P::kTmemAlloc);
+    tmem_relinquish_1();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = tmem_slot;
+
+  WaitCtx wctx;
+  wctx.status = args.status;
+  wctx.timeout_ns = args.timeout_ns;
+  wctx.abort_local = smem_u32(&abort_word);
+  wctx.abort_peer = smem_u32(&abort_word);
+
+  // Segments of [lo, hi): tile t, K blocks [kb0, kb1).
+#define B200_FOR_SEGMENTS(...)                                                \
+  for (long long pos = lo; pos < hi;) {                                       \
+    const int t = (int)(pos / KB);                                            \
+    const int kb0 = (int)(pos - (long long)t * KB);                           \
+    const long long rest = hi - (long long)t * KB;                            \
+    const int kb1 = rest < KB ? (int)rest : KB;                               \
+    __VA_ARGS__                                                               \
+    pos = (long long)t * KB + kb1;                                            \
+  }
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_b = args.l2_hint ? l2_policy_evict_first() : l2_policy_evict_normal();
+      const uint64_t pol_a = args.l2_hint ? l2_policy_evict_last() : l2_policy_evict_normal();
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      B200_FOR_SEGMENTS({
+        for (int kb = kb0; ok && kb < kb1; ++kb) {
+          if (!wait_bounded(smem_u32(&bar_empty[stage]), phase ^ 1u, wctx, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sb = smem_base + stage * P::kStageBytes;
+          const uint32_t fb = smem_u32(&bar_full[stage]);
+          mbar_arrive_expect_tx(fb, P::kStageBytes);
+#pragma unroll
+          for (int sl = 0; sl < kSlabs; ++sl)
+            tma_load_2d_hint(sb + sl * P::kSlabB, &tmap_b, kb * P::kBK + sl * kSlabK,
+                             t * P::kRowsB, fb, pol_b);
+#pragma unroll
+          for (int sl = 0; sl < kSlabs; ++sl)
+            tma_load_2d_hint(sb + P::kBytesB + sl * P::kSlabA, &tmap_a, kb * P::kBK + sl * kSlabK,
+                             0, fb, pol_a);
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+      })
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_bf16_f32(P::kRowsB, kMp);
+      uint32_t stage = 0, phase = 0;
+      int it = 0;
+      bool ok = true;
+      B200_FOR_SEGMENTS({
+        const uint32_t buf = it & 1, acc_phase = (it >> 1) & 1;
+        if (!wait_bounded(smem_u32(&bar_acc_empty[buf]), acc_phase ^ 1u, wctx, kErrWaitAccEmpty))
+          break;
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + buf * kMp;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!wait_bounded(smem_u32(&bar_full[stage]), phase, wctx, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t sb = smem_base + stage * P::kStageBytes;
+#pragma unroll
+          for (int sl = 0; sl < kSlabs; ++sl) {
+            const uint64_t bdesc = make_sdesc_k128(sb + sl * P::kSlabB);
+            const uint64_t adesc = make_sdesc_k128(sb + P::kBytesB + sl * P::kSlabA);
+#pragma unroll
+            for (int k = 0; k < kSlabK / kMmaK; ++k)
+              umma_bf16_1(d_tmem, bdesc + 2ull * k, adesc + 2ull * k, idesc,
+                          (kb != kb0 || sl != 0 || k != 0) ? 1u : 0u);
+          }
+          umma_commit_1(smem_u32(&bar_empty[stage]));
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_1(smem_u32(&bar_acc_full[buf]));
+        ++it;
+      })
+      umma_commit_1(smem_u32(&bar_drain));
+      if (!mbar_try_wait(smem_u32(&bar_drain), 0))
+        wait_slow(smem_u32(&bar_drain), 0, wctx, kErrWaitDrain, false);
+    }
+    __syncwarp();
+  } else {
+    // Epilogue: warp w holds TMEM lanes 32 (w % 4) .. + 31 = rows n of B
+    // (columns of C); register j of a chunk is row m = c kChunk + j of C.
+    const int quarter = warp & 3;
+    const int n_local = quarter * 32 + lane;
+    const uint32_t my_store = store_base + (warp - 2) * 2 * P::kStoreBuf;
+    uint32_t nstore = 0;
+    int it = 0;
+    int fix_tile = -1, fix_slots = 0;  // tile this CTA finishes after its range
+    bool alive = true;
+    // Rounds 32 (or Mp) rows of C held as fp32 bits in v and TMA-stores them
+    // through this warp's staging buffers ([kChunk m][32 n] bf16).
+    auto store_bf16 = [&](const uint32_t* v, int t, int c) {
+      const uint32_t sb = my_store + (nstore & 1u) * P::kStoreBuf;
+      if (lane == 0) bulk_wait_group_read<1>();
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        const __nv_bfloat16 h = __float2bfloat16_rn(__uint_as_float(v[j]));
+        st_shared_u16(sb + (j * 32 + lane) * 2u, *reinterpret_cast<const uint16_t*>(&h));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&tmap_c, sb, t * P::kRowsB + quarter * 32, c * kChunk);
+        bulk_commit_group();
+      }
+      ++nstore;
+    };
+    B200_FOR_SEGMENTS({
+      if (!alive) break;
+      const uint32_t buf = it & 1, acc_phase = (it >> 1) & 1;
+      int ok = 0;
+      if (lane == 0) ok = wait_bounded(smem_u32(&bar_acc_full[buf]), acc_phase, wctx, kErrWaitAccFull);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) {
+        alive = false;
+        break;
+      }
+      tc_fence_after_sync();
+      const uint32_t tbase = tmem_base + buf * kMp + ((uint32_t)(quarter * 32) << 16);
+      const bool whole = kb0 == 0 && kb1 == KB;
+      const int j = (int)blockIdx.x - stream_owner((long long)t * KB, args.total, G);
+      float* slot = args.slots + (((long long)t * args.max_seg + j) * kMp) * P::kRowsB + n_local;
+#pragma unroll 1
+      for (int c = 0; c < kMp / kChunk; ++c) {
+        uint32_t v[kChunk];
+        if constexpr (kChunk == 16)
+          tmem_ld_32x32b_x16(tbase + c * 16, *reinterpret_cast<uint32_t(*)[16]>(v));
+        else
+          tmem_ld_32x32b_x32(tbase + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v));
+        tmem_wait_ld();
+        if (c == kMp / kChunk - 1) {
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_local(smem_u32(&bar_acc_empty[buf]));
+        }
+        if (whole) {
+          store_bf16(v, t, c);
+        } else {
+          // slot[m][n_local]: each warp-wide store covers 128 contiguous bytes
+#pragma unroll
+          for (int jj = 0; jj < kChunk; ++jj)
+            slot[(long long)(c * kChunk + jj) * P::kRowsB] = __uint_as_float(v[jj]);
+        }
+      }
+      if (!whole) {
+        if (kb1 == KB) {
+          fix_tile = t;  // this CTA holds the tile's last K blocks: it finishes it
+          fix_slots = j + 1;
+        } else {
+          asm volatile("fence.acq_rel.gpu;" ::: "memory");
+          __syncwarp();
+          if (lane == 0)
+            st_release_gpu_u32(args.flags + ((long long)t * args.max_seg + j) * 4 + quarter, 1u);
+        }
+      }
+      ++it;
+    })
+    if (alive && fix_tile >= 0) {
+      // Finish the tile: wait for the earlier contributors' slots, add all
+      // slots in K order, round, store.
+      const long long tslots = (long long)fix_tile * args.max_seg;
+      bool ready = true;
+      for (int s = 0; ready && s < fix_slots - 1; ++s) {
+        const unsigned int* f = args.flags + (tslots + s) * 4 + quarter;
+        const unsigned long long t0 = globaltimer_ns();
+        for (;;) {
+          const bool up = ld_acquire_gpu_u32(f) != 0u;
+          if (__all_sync(0xffffffffu, up)) break;
+          int give_up = 0;
+          if (lane == 0 && globaltimer_ns() - t0 > args.timeout_ns) {
+            atomicCAS(args.status, 0, kErrWaitPartial);
+            give_up = 1;
+          }
+          if (__shfl_sync(0xffffffffu, give_up, 0)) {
+            ready = false;
+            break;
+          }
+          __nanosleep(128);
+        }
+      }
+      if (ready) {
+        const float* base = args.slots + tslots * kMp * P::kRowsB + n_local;
+#pragma unroll 1
+        for (int c = 0; c < kMp / kChunk; ++c) {
+          float acc[kChunk];
+#pragma unroll
+          for (int jj = 0; jj < kChunk; ++jj) acc[jj] = 0.f;
+#pragma unroll 1
+          for (int s = 0; s < fix_slots; ++s) {
+            const float* p = base + ((long long)s * kMp + c * kChunk) * P::kRowsB;
+#pragma unroll
+            for (int jj = 0; jj < kChunk; ++jj) acc[jj] += __ldcg(p + (long long)jj * P::kRowsB);
+          }
+          uint32_t v[kChunk];
+#pragma unroll
+          for (int jj = 0; jj < kChunk; ++jj) v[jj] = __float_as_uint(acc[jj]);
+          store_bf16(v, fix_tile, c);
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+#undef B200_FOR_SEGMENTS
 
   tc_fence_before_sync();
   __syncthreads();

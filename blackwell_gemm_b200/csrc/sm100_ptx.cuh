@@ -77,7 +77,10 @@ __device__ __forceinline__ void fence_mbar_init_cluster() {
 // completed sleeps until it does or until this many nanoseconds pass, instead
 // of re-polling.  Polling warps would otherwise take issue slots from the
 // single thread that feeds the tensor core on the same scheduler.
-constexpr uint32_t kPollSuspendNs = 1000000;
+#ifndef B200_POLL_SUSPEND_NS
+#define B200_POLL_SUSPEND_NS 1000000
+#endif
+constexpr uint32_t kPollSuspendNs = B200_POLL_SUSPEND_NS;
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;
@@ -242,6 +245,37 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* m, 
       : "memory");
 }
 
+// L2 eviction policies for cache-hinted loads (PTX createpolicy): data read
+// once is marked evict-first, so streaming it does not push reused or dirty
+// lines out of L2; data every CTA reads again is marked evict-last.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// tma_load_2d with an L2 cache policy.
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* m, int x, int y,
+                                                 uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;"
+      :: "r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_1(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                :: "r"(dst_smem), "r"(ncols) : "memory");
@@ -297,6 +331,10 @@ __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t cluster_addr) {
 
 __device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared.u32 [%0], %1;" :: "r"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" :: "r"(addr), "h"(v) : "memory");
 }
 
 }  // namespace b200

@@ -76,6 +76,14 @@ int b200_cast_f32_bf16(const float* W, int ldw, void* C, int ldc, int M, int N, 
 int b200_gemm_set_splits(int splits);
 int b200_gemm_get_splits(int M, int N, int K, int* splits);
 
+/* Skinny-M path (M <= 256, N >= 1024, K >= 512: C^T = B A^T so the large
+ * operand B feeds the MMA's 128 rows): 0 = off (pair kernels only), 1 =
+ * chosen per shape (default; B200_GEMM_SKINNY overrides), 2 = the
+ * single-launch cluster kernel for every M, 3 = the stream-K kernel for
+ * every M.  Calls with a fused epilogue take the workspace kernel whatever
+ * the mode.  No reference counterpart. */
+int b200_gemm_set_skinny_mode(int mode);
+
 /* Same GEMM with the intra-kernel profiler on (never split).  `profiler` is a device int64
  * buffer of rows x (1 + 4 * num_entries) entries, rows from
  * b200_gemm_profile_rows; row r = block * warps_per_cta + warp (warps per

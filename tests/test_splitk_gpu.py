@@ -181,13 +181,32 @@ def test_k_split_and_row_shard_on_two_gpus():
 
 
 # ------------------------------------------------------- skinny-M kernel
+SKINNY_MODES = {"auto": 1, "cluster": 2, "stream": 3}
+
+
+@pytest.fixture(params=list(SKINNY_MODES))
+def skinny_mode(request):
+    """The skinny path's kernels: chosen per shape, the cluster split-K kernel
+    and the stream-K kernel, each forced for every M."""
+    capi.set_skinny_mode(SKINNY_MODES[request.param])
+    yield request.param
+    capi.set_skinny_mode(1)
+
+
 @pytest.mark.parametrize("M", [1, 16, 17, 32, 50, 64, 100, 128, 200, 256])
-@pytest.mark.parametrize("N,K", [(1024, 512), (1032, 520), (8200, 1000)])
-def test_skinny_kernel_exact_bits(M, N, K):
-    # M <= 256, N >= 1024, K >= 512 take the C^T = B A^T kernel
+@pytest.mark.parametrize("N,K", [(1024, 512), (1032, 520), (8200, 1000), (2048, 8192)])
+def test_skinny_kernel_exact_bits(M, N, K, skinny_mode):
+    # M <= 256, N >= 1024, K >= 512 take the C^T = B A^T kernels
     A, Bt = oracle.exact_inputs(M, N, K, seed=M)
     C = bf16_gemm(dev(A), dev(Bt))
     assert np.array_equal(bits(C), oracle.gemm_bf16(A, Bt))
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 8192, 8192), (100, 3000, 4000), (256, 1024, 65536)])
+def test_skinny_kernels_random(M, N, K, skinny_mode):
+    A, Bt = workloads.make_operands(M, N, K, seed=M + K, weight_std=0.02)
+    C = bf16_gemm(A, Bt)
+    assert parity.passes(parity.metrics(C, A.float() @ Bt.float().T, A, Bt))
 
 
 @pytest.mark.parametrize("splits", [1, 5, 64])
