@@ -791,6 +791,14 @@ GemmArgs base_args(int M, int N, int K, const DeviceState& d, long long* prof, i
   args.prof = prof;
   args.prof_entries = entries;
   args.epi = {1.0f, 0.0f, nullptr, nullptr, 0};
+  // Operand loads are marked evict-last: at 8192^3 (and the projection
+  // shapes) that keeps A and B ahead of the output and of other data in L2
+  // and was measured ~2% faster, at equal power, than the default policy.
+  // B200_GEMM_L2_A / B200_GEMM_L2_B = 0 (normal), 1 (evict-first), 2 (evict-last).
+  static const int l2_a = env_int("B200_GEMM_L2_A", 2, 0, 2);
+  static const int l2_b = env_int("B200_GEMM_L2_B", 2, 0, 2);
+  args.l2_a = l2_a;
+  args.l2_b = l2_b;
   return args;
 }
 

@@ -58,7 +58,15 @@ struct GemmArgs {
   EpiArgs epi;
   // K-split exchange (kOutKsplit only): see ksplit_fused.cuh.
   KsArgs ks;
+  // L2 eviction policy of the A and B loads: 0 normal, 1 evict-first,
+  // 2 evict-last.
+  int l2_a, l2_b;
 };
+
+__device__ __forceinline__ uint64_t l2_policy(int code) {
+  return code == 1 ? l2_policy_evict_first()
+                   : code == 2 ? l2_policy_evict_last() : l2_policy_evict_normal();
+}
 
 // Error codes written to GemmArgs::status by a wait that ran out.
 enum : int {
@@ -413,6 +421,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     if (lane == 0) {
       const uint32_t full_leader = cluster_map(smem_u32(&bar_full[0]), 0);
       const uint32_t empty_peer = cluster_map(smem_u32(&bar_empty[0]), 1);
+      const uint64_t pol_a = l2_policy(args.l2_a), pol_b = l2_policy(args.l2_b);
       uint32_t stage = 0, phase = 0;
       uint32_t filled = 0;  // ring slots this producer has filled so far
       bool ok = true;
@@ -439,11 +448,11 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
 #pragma unroll
           for (int sl = 0; sl < kSlabs; ++sl) {
             const int x = kb * P::kBK + sl * kSlabK;
-            tma_load_2d_pair(sa + sl * kSlabBytes, &tmap_a, x, a_row, fb);
+            tma_load_2d_pair_hint(sa + sl * kSlabBytes, &tmap_a, x, a_row, fb, pol_a);
 #pragma unroll
             for (int sub = 0; sub < kNSub; ++sub)
-              tma_load_2d_pair(sa + P::kBytesA + (sub * kSlabs + sl) * P::kSlabB, &tmap_b, x,
-                               b_row + sub * kSubW, fb);
+              tma_load_2d_pair_hint(sa + P::kBytesA + (sub * kSlabs + sl) * P::kSlabB, &tmap_b,
+                                    x, b_row + sub * kSubW, fb, pol_b);
           }
           if constexpr (kProfile) prof.stop();
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
