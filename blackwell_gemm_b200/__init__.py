@@ -22,8 +22,8 @@ import types
 
 from . import capi  # noqa: F401
 
-__all__ = ["module", "matmul_b200", "profile_matmul_b200", "matmul_b200_epilogue", "profile_rows",
-           "capi", "load"]
+__all__ = ["module", "matmul_b200", "profile_matmul_b200", "matmul_b200_epilogue",
+           "matmul_b200_host", "profile_rows", "capi", "load"]
 
 _ext = None
 
@@ -113,6 +113,39 @@ def matmul_b200_epilogue(A, B, *, alpha: float = 1.0, bias=None, beta: float = 1
                                      torch.cuda.current_stream(A.device).cuda_stream)
     capi.check(st, "matmul_b200_epilogue")
     return Cbuf[:, :N] if ldc == N else Cbuf[:, :N].contiguous()
+
+
+def matmul_b200_host(A, B, *, block_rows: int = 0, out=None):
+    """C = A @ B for operands in host memory (CPU bf16 tensors; page-locked
+    memory lets the transfers overlap).  A: (M, K); B: (K, N), normally the .T
+    of an (N, K) tensor.  B is copied to the current CUDA device once, A is
+    streamed in blocks of rows with uploads, GEMMs and downloads overlapped
+    (b200_gemm_bf16_host).  Returns `out` or a new page-locked (M, N) tensor;
+    waits for the result."""
+    import torch
+
+    if A.dim() != 2 or B.dim() != 2 or B.shape[0] != A.shape[1]:
+        raise RuntimeError("matmul_b200_host: A must be (M, K) and B (K, N)")
+    for t in (A, B):
+        if t.is_cuda or t.dtype != torch.bfloat16:
+            raise RuntimeError("matmul_b200_host: A and B must be bfloat16 CPU tensors")
+    M, K = A.shape
+    N = B.shape[1]
+    a = A if A.stride(1) == 1 else A.contiguous()
+    bt = B.t()
+    if bt.stride(1) != 1:
+        bt = bt.contiguous()
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+    if out.shape != (M, N) or out.stride(1) != 1:
+        raise RuntimeError("matmul_b200_host: out must be a row-major (M, N) tensor")
+    stream = torch.cuda.current_stream()
+    st = capi.gemm_bf16_host(a.data_ptr(), bt.data_ptr(), out.data_ptr(), M, N, K,
+                             a.stride(0) if M > 1 else K, bt.stride(0) if N > 1 else K,
+                             out.stride(0) if M > 1 else N, block_rows, stream.cuda_stream)
+    capi.check(st, "matmul_b200_host")
+    stream.synchronize()
+    return out
 
 
 def profile_rows(M: int, N: int, K: int) -> int:

@@ -45,6 +45,7 @@ SIGNATURES = {
     "b200_gemm_bf16_f32out": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "b200_gemm_bf16_noalloc": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "b200_cast_f32_bf16": (_i, [_vp, _i, _vp, _i, _i, _i, _vp]),
+    "b200_gemm_bf16_host": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "b200_gemm_bf16_epilogue": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, ctypes.c_float, _vp,
                                      ctypes.c_float, _vp, _i, _vp]),
     "b200_gemm_set_splits": (_i, [_i]),
@@ -118,6 +119,14 @@ def gemm_bf16_epilogue(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, alpha, bias_
     return lib().b200_gemm_bf16_epilogue(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc,
                                          float(alpha), bias_ptr or None, float(beta),
                                          resid_ptr or None, ldr, stream)
+
+
+def gemm_bf16_host(a_ptr: int, b_ptr: int, c_ptr: int, M: int, N: int, K: int, lda: int,
+                   ldb: int, ldc: int, block_rows: int = 0, stream: int = 0) -> int:
+    """b200_gemm_bf16_host: host pointers (pinned for overlap), asynchronous on
+    `stream`."""
+    return lib().b200_gemm_bf16_host(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, block_rows,
+                                     stream)
 
 
 def cast_f32_bf16(w_ptr: int, ldw: int, c_ptr: int, ldc: int, M: int, N: int,

@@ -880,6 +880,136 @@ int run_gemm_f32out(const void* A, const void* B, float* C, int M, int N, int K,
 }
 
 // ---------------------------------------------------------------------------
+// Host-resident operands: B goes to the device once, A streams in blocks of
+// rows.  Block i's upload, GEMM and the download of its rows of C run on three
+// streams of their own, so uploads, GEMMs and downloads of different blocks
+// overlap (the link carries data in both directions at once).  Three device
+// buffers per operand block rotate; events order buffer reuse.  The whole
+// pipeline is ordered after the caller's stream at entry and the caller's
+// stream waits for its end, so the call is asynchronous like the others.
+struct HostPipe {
+  bool ready = false;
+  cudaStream_t up = nullptr, mm = nullptr, down = nullptr;
+};
+HostPipe g_pipe[kMaxDevices];
+
+int host_pipe(HostPipe** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return B200_ERR_UNSUPPORTED_DEVICE;
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  HostPipe& p = g_pipe[dev];
+  if (!p.ready) {
+    if (cudaStreamCreateWithFlags(&p.up, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&p.mm, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&p.down, cudaStreamNonBlocking) != cudaSuccess) {
+      cudaGetLastError();
+      return B200_ERR_LAUNCH;
+    }
+    p.ready = true;
+  }
+  *out = &p;
+  return B200_OK;
+}
+
+int run_gemm_host(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
+                  int ldc, int block_rows, cudaStream_t stream) {
+  if (M < 0 || N < 0 || K < 0 || block_rows < 0) return B200_ERR_INVALID_ARGUMENT;
+  if (M == 0 || N == 0) return B200_OK;
+  if (!C || (K > 0 && (!A || !B)) || ldc < N || (K > 0 && (lda < K || ldb < K)))
+    return B200_ERR_INVALID_ARGUMENT;
+  DeviceState* d = nullptr;
+  int st = device_state(&d);
+  if (st != B200_OK) return st;
+  HostPipe* p = nullptr;
+  st = host_pipe(&p);
+  if (st != B200_OK) return st;
+  if (block_rows == 0) {
+    block_rows = (int)(ceil_div(ceil_div(M, 8), kPairM) * kPairM);
+    if (block_rows < kPairM) block_rows = kPairM;
+  }
+  if (block_rows > M) block_rows = M;
+  const int blocks = (int)ceil_div(M, block_rows);
+  constexpr int kBufs = 3;
+  const int nb = blocks < kBufs ? blocks : kBufs;
+  const int kd = (int)ceil_div(K > 0 ? K : 1, 8) * 8;  // device row strides: 16-byte multiples
+  const int nd = (int)ceil_div(N, 8) * 8;
+  const size_t b_bytes = (size_t)N * kd * 2;
+  const size_t a_bytes = (size_t)block_rows * kd * 2;
+  const size_t c_bytes = (size_t)block_rows * nd * 2;
+  const size_t total = b_bytes + nb * (a_bytes + c_bytes);
+
+  const int nev = 2 + 3 * blocks;
+  cudaEvent_t* ev = new cudaEvent_t[nev];
+  int made = 0;
+  for (; made < nev; ++made)
+    if (cudaEventCreateWithFlags(&ev[made], cudaEventDisableTiming) != cudaSuccess) break;
+  auto finish = [&](int status) {
+    for (int i = 0; i < made; ++i) cudaEventDestroy(ev[i]);
+    delete[] ev;
+    if (status != B200_OK) cudaGetLastError();
+    return status;
+  };
+  if (made < nev) return finish(B200_ERR_LAUNCH);
+  cudaEvent_t ev_start = ev[0], ev_end = ev[1];
+  cudaEvent_t* ev_up = ev + 2;               // block i uploaded
+  cudaEvent_t* ev_mm = ev + 2 + blocks;      // block i's GEMM done
+  cudaEvent_t* ev_down = ev + 2 + 2 * blocks;  // block i's rows of C downloaded
+
+  bool ok = cudaEventRecord(ev_start, stream) == cudaSuccess &&
+            cudaStreamWaitEvent(p->up, ev_start, 0) == cudaSuccess &&
+            cudaStreamWaitEvent(p->mm, ev_start, 0) == cudaSuccess &&
+            cudaStreamWaitEvent(p->down, ev_start, 0) == cudaSuccess;
+  char* ws = nullptr;
+  if (ok) ok = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), total, d->pool, p->up) ==
+               cudaSuccess;
+  if (!ok) return finish(B200_ERR_LAUNCH);
+  char* dB = ws;
+  char* dA = ws + b_bytes;
+  char* dC = dA + nb * a_bytes;
+  if (K > 0)
+    ok = cudaMemcpy2DAsync(dB, (size_t)kd * 2, B, (size_t)ldb * 2, (size_t)K * 2, N,
+                           cudaMemcpyHostToDevice, p->up) == cudaSuccess;
+  for (int i = 0; ok && i < blocks; ++i) {
+    const int r0 = i * block_rows;
+    const int rows = M - r0 < block_rows ? M - r0 : block_rows;
+    const int b = i % nb;
+    char* a = dA + b * a_bytes;
+    char* c = dC + b * c_bytes;
+    // upload A block i once the GEMM that last read this buffer is done
+    if (i >= nb) ok = cudaStreamWaitEvent(p->up, ev_mm[i - nb], 0) == cudaSuccess;
+    if (ok && K > 0)
+      ok = cudaMemcpy2DAsync(a, (size_t)kd * 2, static_cast<const char*>(A) + (size_t)r0 * lda * 2,
+                             (size_t)lda * 2, (size_t)K * 2, rows, cudaMemcpyHostToDevice,
+                             p->up) == cudaSuccess;
+    ok = ok && cudaEventRecord(ev_up[i], p->up) == cudaSuccess &&
+         cudaStreamWaitEvent(p->mm, ev_up[i], 0) == cudaSuccess;
+    // the GEMM writes C buffer b once its previous rows have been downloaded
+    if (ok && i >= nb) ok = cudaStreamWaitEvent(p->mm, ev_down[i - nb], 0) == cudaSuccess;
+    if (ok) ok = run_gemm<false>(a, dB, c, rows, N, K, kd, kd, nd, nullptr, 0, p->mm) == B200_OK;
+    ok = ok && cudaEventRecord(ev_mm[i], p->mm) == cudaSuccess &&
+         cudaStreamWaitEvent(p->down, ev_mm[i], 0) == cudaSuccess &&
+         cudaMemcpy2DAsync(static_cast<char*>(C) + (size_t)r0 * ldc * 2, (size_t)ldc * 2, c,
+                           (size_t)nd * 2, (size_t)N * 2, rows, cudaMemcpyDeviceToHost,
+                           p->down) == cudaSuccess &&
+         cudaEventRecord(ev_down[i], p->down) == cudaSuccess;
+  }
+  // Join: the download stream follows the other two, frees the buffers and
+  // releases the caller's stream.
+  if (ok)
+    ok = cudaEventRecord(ev_up[blocks - 1], p->up) == cudaSuccess &&
+         cudaStreamWaitEvent(p->down, ev_up[blocks - 1], 0) == cudaSuccess &&
+         cudaEventRecord(ev_mm[blocks - 1], p->mm) == cudaSuccess &&
+         cudaStreamWaitEvent(p->down, ev_mm[blocks - 1], 0) == cudaSuccess;
+  cudaFreeAsync(ws, p->down);
+  ok = ok && cudaEventRecord(ev_end, p->down) == cudaSuccess &&
+       cudaStreamWaitEvent(stream, ev_end, 0) == cudaSuccess;
+  return finish(ok ? B200_OK : B200_ERR_LAUNCH);
+}
+
+// ---------------------------------------------------------------------------
 // Fused K-split over NVLink (device side: ksplit_fused.cuh).
 //
 // Exchange blob (B200_KSPLIT_HANDLE_BYTES) that each rank publishes: the IPC
@@ -1022,6 +1152,12 @@ int b200_gemm_bf16_epilogue(const void* A, const void* B, void* C, int M, int N,
                        static_cast<const __nv_bfloat16*>(residual), ldr};
   return run_gemm<false>(A, B, C, M, N, K, lda, ldb, ldc, nullptr, 0,
                          static_cast<cudaStream_t>(stream), &epi);
+}
+
+int b200_gemm_bf16_host(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                        int ldb, int ldc, int block_rows, void* stream) {
+  return run_gemm_host(A, B, C, M, N, K, lda, ldb, ldc, block_rows,
+                       static_cast<cudaStream_t>(stream));
 }
 
 int b200_cast_f32_bf16(const float* W, int ldw, void* C, int ldc, int M, int N, void* stream) {

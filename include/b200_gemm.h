@@ -62,6 +62,21 @@ int b200_gemm_bf16_epilogue(const void* A, const void* B, void* C, int M, int N,
                             int ldb, int ldc, float alpha, const void* bias, float beta,
                             const void* residual, int ldr, void* stream);
 
+/* The same GEMM on operands in HOST memory (A, B and C host pointers; page-
+ * locked memory lets the transfers run asynchronously and overlap).  B is
+ * copied to the device once per call; A is streamed in blocks of block_rows
+ * rows (0 = chosen: M / 8 rounded up to 256); each block's upload, GEMM and
+ * the download of its rows of C run on three internal streams, so uploads,
+ * GEMMs and downloads of different blocks overlap and the link moves data in
+ * both directions at once.  Device buffers (B plus three blocks of A and of
+ * C) come from the library's per-device pool.  Ordered after the work
+ * already on `stream`, and `stream` waits for the result: the host buffers
+ * must stay valid until then.  Strides as for b200_gemm_bf16 (no alignment
+ * rule on the host side).  No reference counterpart (the reference takes
+ * device tensors; its harness copies them serially). */
+int b200_gemm_bf16_host(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                        int ldb, int ldc, int block_rows, void* stream);
+
 /* bf16 C = round-to-nearest-even(W) for an fp32 M x N matrix W (row stride
  * ldw floats, a multiple of 4; C row stride ldc, a multiple of 8).  The last
  * step of a K-split GEMM after the partials are summed.  No reference
