@@ -50,6 +50,7 @@ SIGNATURES = {
                                      ctypes.c_float, _vp, _i, _vp]),
     "b200_gemm_set_splits": (_i, [_i]),
     "b200_gemm_set_skinny_mode": (_i, [_i]),
+    "b200_gemm_set_stream_k": (_i, [_i]),
     "b200_gemm_get_splits": (_i, [_i, _i, _i, _ip]),
     "b200_gemm_profile_rows": (_i, [_i, _i, _i, _ip]),
     "b200_gemm_device_status": (_i, [_i, _ip]),
@@ -143,6 +144,11 @@ def gemm_bf16_noalloc(a_ptr: int, b_ptr: int, c_ptr: int, M: int, N: int, K: int
 
 def set_splits(splits: int) -> None:
     check(lib().b200_gemm_set_splits(int(splits)), "set_splits")
+
+
+def set_stream_k(mode: int) -> None:
+    """0 off, 1 when the last wave is short (default), 2 whenever it is partial."""
+    check(lib().b200_gemm_set_stream_k(mode), "b200_gemm_set_stream_k")
 
 
 def set_skinny_mode(mode: int) -> None:

@@ -60,9 +60,9 @@ struct VariantCfg {
   using C = Cfg<kVariantSlabs[V], kVariantNSub[V], kVariantSubW[V]>;
 };
 
-template <bool kProfile, int V, int kOut>
+template <bool kProfile, int V, int kOut, bool kSK = false>
 constexpr auto pair_kernel =
-    gemm_bf16_pair_kernel<kProfile, kVariantSlabs[V], kVariantNSub[V], kOut, kVariantSubW[V]>;
+    gemm_bf16_pair_kernel<kProfile, kVariantSlabs[V], kVariantNSub[V], kOut, kVariantSubW[V], kSK>;
 
 constexpr int kMaxDevices = 64;
 
@@ -96,6 +96,23 @@ std::atomic<int> g_slabs{-1};
 std::atomic<int> g_group{0};
 std::atomic<int> g_splits{-1};
 std::atomic<int> g_skinny{-1};
+std::atomic<int> g_streamk{-1};
+
+// Below this wave efficiency a 256 x 256 grid gets a stream-K tail (mode 1).
+constexpr double kStreamKWaveEfficiency = 0.97;
+
+// Stream-K tail of the pair kernel: 0 = off, 1 = when the last wave of tiles
+// would leave pairs idle (default), 2 = whenever the tiles are not a whole
+// number of waves.  Initialised from B200_GEMM_STREAMK, changeable through
+// b200_gemm_set_stream_k.
+int stream_k_mode() {
+  int v = g_streamk.load();
+  if (v < 0) {
+    v = env_int("B200_GEMM_STREAMK", 1, 0, 2);
+    g_streamk.store(v);
+  }
+  return v;
+}
 
 // L2 cache hints of the skinny kernels' loads (B200_GEMM_L2_HINT, default 1):
 // B, read once, evict-first; A, read by every CTA, evict-last.
@@ -175,9 +192,9 @@ int query_pairs(int sms, int* out) {
   return B200_OK;
 }
 
-template <bool kProfile, int V, int kOut>
+template <bool kProfile, int V, int kOut, bool kSK = false>
 bool set_smem_limit() {
-  return cudaFuncSetAttribute(pair_kernel<kProfile, V, kOut>,
+  return cudaFuncSetAttribute(pair_kernel<kProfile, V, kOut, kSK>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                               VariantCfg<V>::C::kSmemBytes) == cudaSuccess;
 }
@@ -192,7 +209,8 @@ bool set_smem_limits() {
 int init_variants(int sms, int* max_pairs) {
   if (!set_smem_limits<kV256x64>() || !set_smem_limits<kV256x128>() ||
       !set_smem_limits<kV512x64>() || !set_smem_limits<kV128x64>() ||
-      !set_smem_limits<kV64x64>())
+      !set_smem_limits<kV64x64>() || !set_smem_limit<false, kV256x64, kOutBf16, true>() ||
+      !set_smem_limit<false, kV256x128, kOutBf16, true>())
     return B200_ERR_LAUNCH;
   if (query_pairs<kV256x64>(sms, &max_pairs[kV256x64]) != B200_OK ||
       query_pairs<kV256x128>(sms, &max_pairs[kV256x128]) != B200_OK ||
@@ -363,9 +381,13 @@ int choose_variant(int M, int N, const int* max_pairs) {
     return best;
   }
   if (t512 < pairs(kV512x64)) return v256;
-  return wave_efficiency(t512, pairs(kV512x64)) + 0.02 >= wave_efficiency(t256, pairs(v256))
-             ? kV512x64
-             : v256;
+  // A 256-wide grid whose last wave would run a stream-K tail keeps every
+  // pair busy to the end: count it as (nearly) full.
+  double eff256 = wave_efficiency(t256, pairs(v256));
+  if (stream_k_mode() != 0 && t256 > pairs(v256) && t256 % pairs(v256) != 0 &&
+      (stream_k_mode() == 2 || eff256 < kStreamKWaveEfficiency))
+    eff256 = 0.99;
+  return wave_efficiency(t512, pairs(kV512x64)) + 0.02 >= eff256 ? kV512x64 : v256;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -432,7 +454,7 @@ int choose_splits(int M, int N, int k_blocks, int pairs) {
   return s < 1 ? 1 : s;
 }
 
-template <bool kProfile, int V, int kOut>
+template <bool kProfile, int V, int kOut, bool kSK = false>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmArgs args,
            int splits, const DeviceState& d, cudaStream_t stream) {
   using C = typename VariantCfg<V>::C;
@@ -441,20 +463,137 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
   if (splits > args.k_blocks) splits = args.k_blocks;
   args.kb_per_split = (int)ceil_div(args.k_blocks, splits);
   args.splits = (int)ceil_div(args.k_blocks, args.kb_per_split);  // every slice non-empty
-  const long long units = (long long)args.tiles_m * args.tiles_n * args.splits;
+  if (args.sk_tiles <= 0) {
+    args.sk_tiles = 0;
+    args.dp_tiles = args.tiles_m * args.tiles_n;
+  }
+  const long long units =
+      args.sk_tiles > 0 ? d.max_pairs[V] : (long long)args.dp_tiles * args.splits;
   const int pairs = (int)(units < d.max_pairs[V] ? units : d.max_pairs[V]);
-  pair_kernel<kProfile, V, kOut><<<2 * pairs, C::kThreads, C::kSmemBytes, stream>>>(ta, tb, tc,
-                                                                                   args);
+  pair_kernel<kProfile, V, kOut, kSK><<<2 * pairs, C::kThreads, C::kSmemBytes, stream>>>(
+      ta, tb, tc, args);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
 }
 
 // bf16 GEMM with configuration v.  tb maps B with 128-row boxes (the
 // 256-wide sub-tiles); narrower sub-tiles load kSubW / 2 rows of B per CTA,
 // so their map is encoded here.
+// Per-(device, stream) stream-K flag arrays and their epochs.  Returns the
+// array (at least `count` flags, zeroed when created) and the next epoch in
+// *epoch, or null when one cannot be made (the caller then clears flags of
+// its own).  Arrays live until exit.
+struct StreamFlags {
+  int device;
+  cudaStream_t stream;
+  unsigned int* flags;
+  size_t count;
+  unsigned int epoch;
+};
+constexpr int kMaxStreamFlags = 256;
+StreamFlags g_stream_flags[kMaxStreamFlags];
+int g_num_stream_flags = 0;
+
+unsigned int* stream_flags(cudaStream_t stream, size_t count, unsigned int* epoch) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  for (int i = 0; i < g_num_stream_flags; ++i) {
+    StreamFlags& f = g_stream_flags[i];
+    if (f.device == dev && f.stream == stream && f.count >= count) {
+      if (++f.epoch == 0) return nullptr;  // 2^32 calls: fall back to cleared flags
+      *epoch = f.epoch;
+      return f.flags;
+    }
+  }
+  if (g_num_stream_flags == kMaxStreamFlags) return nullptr;
+  const size_t n = count < 4096 ? 4096 : count;
+  unsigned int* p = nullptr;
+  // cudaMalloc + a blocking clear, once per stream: the array starts at epoch 0.
+  if (cudaMalloc(&p, n * sizeof(unsigned int)) != cudaSuccess ||
+      cudaMemset(p, 0, n * sizeof(unsigned int)) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess) {
+    cudaGetLastError();
+    if (p) cudaFree(p);
+    return nullptr;
+  }
+  g_stream_flags[g_num_stream_flags++] = {dev, stream, p, n, 1u};
+  *epoch = 1u;
+  return p;
+}
+
+// Data-parallel waves plus a stream-K tail (see GemmArgs): applies to the
+// 256 x 256 pair-tile configurations (their second TMEM accumulator lets a
+// tile's finishing epilogue overlap the next tile's MMAs) when the tiles are
+// more than one wave and not a whole number of waves (mode 1: only when the last wave would leave
+// at least 3 % of the pair-slots idle).  Sets *used; the workspace (one
+// piece per epilogue warp per pair, and their flags) comes from the pool.
+template <int V>
+int launch_streamk(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                   GemmArgs args, const DeviceState& d, cudaStream_t stream, bool* used) {
+  using C = typename VariantCfg<V>::C;
+  *used = false;
+  const int mode = stream_k_mode();
+  if (mode == 0) return B200_OK;
+  const long long tiles = (long long)args.tiles_m * ceil_div(args.N, C::kTileN);
+  const int P = d.max_pairs[V];
+  if (tiles <= P || tiles % P == 0) return B200_OK;
+  if (mode == 1 && wave_efficiency(tiles, P) >= kStreamKWaveEfficiency) return B200_OK;
+  const long long k_blocks = ceil_div(args.K, C::kBK);
+  args.dp_tiles = (int)(tiles / P * P);
+  args.sk_tiles = (int)(tiles - args.dp_tiles);
+  args.sk_items = args.sk_tiles * k_blocks;
+  const long long slots = (long long)P * 2 * C::kEpiWarps;  // one piece per epilogue warp per pair
+  const size_t flag_bytes = (size_t)ceil_div(slots * 4, 256) * 256;
+  const size_t slot_bytes = (size_t)slots * kPieceFloats * sizeof(float);
+  char* ws = nullptr;
+  if (cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), flag_bytes + slot_bytes, d.pool,
+                              stream) != cudaSuccess) {
+    cudaGetLastError();
+    return B200_ERR_LAUNCH;
+  }
+  args.sk_slots = reinterpret_cast<float*>(ws + flag_bytes);
+  // Flags: outside stream capture, a per-(device, stream) array that keeps
+  // its values between calls, each call raising flags to a new epoch (stale
+  // flags hold older epochs, so nothing needs clearing and no extra
+  // operation precedes the kernel; calls on one stream are ordered, calls on
+  // different streams use different arrays).  Under capture the graph may be
+  // replayed with the same epoch, so the workspace's own flags are cleared
+  // in the graph instead.
+  int st = B200_OK;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+    cudaGetLastError();
+    cap = cudaStreamCaptureStatusActive;
+  }
+  unsigned int* persistent = nullptr;
+  if (cap == cudaStreamCaptureStatusNone)
+    persistent = stream_flags(stream, (size_t)slots, &args.sk_epoch);
+  if (persistent != nullptr) {
+    args.sk_flags = persistent;
+  } else {
+    args.sk_flags = reinterpret_cast<unsigned int*>(ws);
+    args.sk_epoch = 1;
+    if (cudaMemsetAsync(ws, 0, flag_bytes, stream) != cudaSuccess) st = B200_ERR_LAUNCH;
+  }
+  if (st == B200_OK) st = launch<false, V, kOutBf16, true>(ta, tb, tc, args, 1, d, stream);
+  cudaFreeAsync(ws, stream);
+  *used = true;
+  return st;
+}
+
 template <bool kProfile>
 int launch_bf16(int v, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                 const void* B, int ldb, const GemmArgs& args, const DeviceState& d,
                 cudaStream_t stream) {
+  if (!kProfile && (v == kV256x64 || v == kV256x128)) {
+    bool used = false;
+    const int st = v == kV256x128 ? launch_streamk<kV256x128>(ta, tb, tc, args, d, stream, &used)
+                                  : launch_streamk<kV256x64>(ta, tb, tc, args, d, stream, &used);
+    if (used || st != B200_OK) return st;
+  }
   if (v == kV128x64 || v == kV64x64) {
     CUtensorMap tbn;
     if (encode_2d(&tbn, B, args.K, args.N, ldb, kSlabK, kVariantSubW[v] / 2) != B200_OK)
@@ -791,6 +930,12 @@ GemmArgs base_args(int M, int N, int K, const DeviceState& d, long long* prof, i
   args.prof = prof;
   args.prof_entries = entries;
   args.epi = {1.0f, 0.0f, nullptr, nullptr, 0};
+  args.dp_tiles = 0;
+  args.sk_tiles = 0;
+  args.sk_items = 0;
+  args.sk_slots = nullptr;
+  args.sk_flags = nullptr;
+  args.sk_epoch = 0;
   // Operand loads are marked evict-last: at 8192^3 (and the projection
   // shapes) that keeps A and B ahead of the output and of other data in L2
   // and was measured ~2% faster, at equal power, than the default policy.
@@ -1229,6 +1374,12 @@ int b200_gemm_set_tuning(int tile_n, int stage_slabs, int raster_group) {
   else if (tile_n != 0) g_tile_n.store(tile_n);
   if (stage_slabs > 0) g_slabs.store(stage_slabs);
   if (raster_group != 0) g_group.store(raster_group);
+  return B200_OK;
+}
+
+int b200_gemm_set_stream_k(int mode) {
+  if (mode < 0 || mode > 2) return B200_ERR_INVALID_ARGUMENT;
+  g_streamk.store(mode);
   return B200_OK;
 }
 

@@ -61,6 +61,19 @@ struct GemmArgs {
   // L2 eviction policy of the A and B loads: 0 normal, 1 evict-first,
   // 2 evict-last.
   int l2_a, l2_b;
+  // Work split.  Tiles [0, dp_tiles) (x splits) are dealt whole, pair p
+  // taking units p, p + P, ...; a stream-K tail of sk_tiles further tiles is
+  // cut into sk_items = sk_tiles x k_blocks (tile, K block) items, pair p
+  // taking the contiguous range [p items / G, (p+1) items / G) (G = min(P,
+  // items)) and walking it from its end.  A tile cut between pairs is finished by the pair
+  // holding its last K blocks -- the first segment of that pair's range,
+  // which it reaches last -- by adding the fp32 pieces the earlier pairs
+  // left in sk_slots to its accumulator (bf16 output only).
+  int dp_tiles, sk_tiles;
+  long long sk_items;
+  float* sk_slots;          // [pair][pieces][kPieceFloats]: the pair's piece of a tile it does not finish
+  unsigned int* sk_flags;   // [pair][pieces], below sk_epoch at launch
+  unsigned int sk_epoch;    // value a raised flag takes in this call
 };
 
 __device__ __forceinline__ uint64_t l2_policy(int code) {
@@ -212,12 +225,15 @@ __device__ __forceinline__ void epi_apply(uint32_t (&v)[32], const EpiArgs& e, i
 // peer's piece.  Gives up when the pair's abort word is set or after
 // timeout_ns (records kErrWaitPeer and raises both abort words); the verdict
 // is warp-uniform.
+template <bool kSys = true>
 __device__ __noinline__ bool wait_peer_flag(const unsigned int* flag, unsigned int epoch,
-                                            const WaitCtx& w, unsigned long long timeout_ns) {
+                                            const WaitCtx& w, unsigned long long timeout_ns,
+                                            int code = kErrWaitPeer) {
   const int lane = threadIdx.x & 31;
   unsigned long long t0 = 0;
   for (int round = 0;; ++round) {
-    const bool ok = (int)(ld_acquire_sys_u32(flag) - epoch) >= 0;
+    const unsigned int v = kSys ? ld_acquire_sys_u32(flag) : ld_acquire_gpu_u32(flag);
+    const bool ok = (int)(v - epoch) >= 0;
     if (__all_sync(0xffffffffu, ok)) return true;
     int give_up = 0;
     if (lane == 0) {
@@ -226,7 +242,7 @@ __device__ __noinline__ bool wait_peer_flag(const unsigned int* flag, unsigned i
       if (ld_volatile_shared(w.abort_local) != 0) {
         give_up = 1;
       } else if (now - t0 > timeout_ns) {
-        atomicCAS(w.status, 0, kErrWaitPeer);
+        atomicCAS(w.status, 0, code);
         asm volatile("st.volatile.shared.u32 [%0], %1;" ::"r"(w.abort_local), "r"(1u) : "memory");
         st_cluster_u32(w.abort_peer, 1u);
         give_up = 1;
@@ -285,10 +301,12 @@ __device__ __forceinline__ long long ks_piece(const KsArgs& ks, int tm, int cb, 
   return ((long long)((tm - *owner * ks.tiles_m_own) * cblocks + cb) * 2 + cta) * 4 + quarter;
 }
 
-// K-split exchange, another owner's tile: write this warp's piece (TMEM
-// columns tbase .. tbase + 255, fp32) into `dst` (the owner's slot, piece
-// layout), hand the accumulator back after its last column, then raise
-// `flag` to `epoch` once every lane's stores are visible system-wide.
+// K-split exchange, another owner's tile (and stream-K partial tiles): write
+// this warp's piece (TMEM columns tbase .. tbase + 255, fp32) into `dst`
+// (piece layout), hand the accumulator back after its last column, then --
+// unless `flag` is null -- raise `flag` to `epoch` once every lane's stores
+// are visible system-wide.
+template <bool kSys = true>
 __device__ __forceinline__ void ks_send_piece(uint32_t tbase, float* dst, unsigned int* flag,
                                               unsigned int epoch, uint32_t acc_empty) {
   const int lane = threadIdx.x & 31;
@@ -307,9 +325,40 @@ __device__ __forceinline__ void ks_send_piece(uint32_t tbase, float* dst, unsign
     for (int j = 0; j < 8; ++j)
       st_global_v4(dst + (c * 8 + j) * 128, v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   }
-  fence_acq_rel_sys();
-  __syncwarp();
-  if (lane == 0) st_release_sys_u32(flag, epoch);
+  if (flag == nullptr) return;
+  if constexpr (kSys) {
+    fence_acq_rel_sys();
+    __syncwarp();
+    if (lane == 0) st_release_sys_u32(flag, epoch);
+  } else {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) st_release_gpu_u32(flag, epoch);
+  }
+}
+
+// Stream-K tail tile: v (this pair's fp32 partial, columns 32h .. 32h+31 of
+// this lane's row) <- P_c0 + P_c0+1 + ... + P_last + v, the earlier pairs'
+// pieces in K order then this pair's own.  `piece` points at this lane's
+// float4 of pair c0's piece; pair c's is (c - c0) * stride floats further.
+__device__ __forceinline__ void sk_accumulate(uint32_t (&v)[32], const float* piece,
+                                              long long stride, int heads, int h) {
+  float s[32];
+#pragma unroll 1
+  for (int c = 0; c < heads; ++c) {
+    const float* p = piece + c * stride + h * 8 * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 x = ld_global_cg_v4(p + j * 128);
+      if (c == 0) {
+        s[4 * j] = x.x; s[4 * j + 1] = x.y; s[4 * j + 2] = x.z; s[4 * j + 3] = x.w;
+      } else {
+        s[4 * j] += x.x; s[4 * j + 1] += x.y; s[4 * j + 2] += x.z; s[4 * j + 3] += x.w;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(s[j] + __uint_as_float(v[j]));
 }
 
 // Work unit u -> tile (tm, tn) and its K-block range [kb0, kb1).  In the
@@ -335,12 +384,72 @@ __device__ __forceinline__ void unit_coord(int u, const GemmArgs& a, int* tm, in
   *kb1 = end < a.k_blocks ? end : a.k_blocks;
 }
 
+// First pair (of G) whose stream-K range [p items / G, (p+1) items / G)
+// holds item x.
+__device__ __forceinline__ int sk_owner(long long x, long long items, int G) {
+  return (int)(((x + 1) * G + items - 1) / items) - 1;
+}
+
+// Pairs taking stream-K work: all P, or one per item when there are fewer
+// items, so that no range is empty.
+__device__ __forceinline__ int sk_pairs(const GemmArgs& a, int P) {
+  return a.sk_items < P ? (int)a.sk_items : P;
+}
+
+// One pair's work, in order: its stream-K segments (a tile and a K-block
+// range within it), last tile first, then its data-parallel units.  Walking
+// the stream-K range backwards makes a pair compute the head of the tile it
+// shares with the next pair first and the tail of the tile it finishes last;
+// doing the stream-K work before the whole tiles lets that tail's epilogue
+// (which adds the heads) overlap the next tile's MMAs.
+struct WorkIter {
+  int u, dp_units, npairs;
+  long long lo, pos;  // stream-K range still to walk: [lo, pos)
+  __device__ __forceinline__ void init(const GemmArgs& a, int pair, int P) {
+    npairs = P;
+    u = pair;
+    dp_units = a.dp_tiles * a.splits;
+    lo = pos = 0;
+    const int G = sk_pairs(a, P);
+    if (a.sk_tiles > 0 && pair < G) {
+      lo = (long long)pair * a.sk_items / G;
+      pos = (long long)(pair + 1) * a.sk_items / G;
+    }
+  }
+  // Next work: tile (tm, tn), K blocks [kb0, kb1), stream-K tile index sk_t
+  // (-1 for a data-parallel unit).  False when the pair's work is done.
+  template <int kOut, bool kSK>
+  __device__ __forceinline__ bool next(const GemmArgs& a, int* tm, int* tn, int* kb0, int* kb1,
+                                       int* sk_t) {
+    if constexpr (kSK) {
+      if (pos > lo) {
+        const int KB = a.k_blocks;
+        const int t = (int)((pos - 1) / KB);
+        const long long base = (long long)t * KB;
+        *kb1 = (int)(pos - base);
+        *kb0 = lo > base ? (int)(lo - base) : 0;
+        tile_coord(a.dp_tiles + t, a.tiles_m, a.tiles_n, a.group, tm, tn);
+        *sk_t = t;
+        pos = base + *kb0;
+        return true;
+      }
+    }
+    if (u < dp_units) {
+      unit_coord<kOut>(u, a, tm, tn, kb0, kb1);
+      *sk_t = -1;
+      u += npairs;
+      return true;
+    }
+    return false;
+  }
+};
+
 __device__ __forceinline__ uint32_t pack_bf16x2(uint32_t lo, uint32_t hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(lo), __uint_as_float(hi));
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <bool kProfile, int kSlabs, int kNSub, int kOut, int kSubW = kSubN>
+template <bool kProfile, int kSlabs, int kNSub, int kOut, int kSubW = kSubN, bool kSK = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<kSlabs, kNSub, kSubW>::kThreads, 1)
 gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
@@ -350,6 +459,9 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
   static_assert(kOut == kOutBf16 || kOut == kOutKsplit || kNSub == 1,
                 "fp32 outputs and fused epilogues use 256-wide pair tiles");
   static_assert(kSubW == kSubN || kOut == kOutBf16, "narrow sub-tiles: plain bf16 output only");
+  static_assert(!kSK || (kOut == kOutBf16 && kSubW == kSubN && kNSub == 1 && !kProfile),
+                "stream-K tails: 256 x 256 pair tiles (double-buffered TMEM), bf16 output, "
+                "no profiler");
   constexpr int kStages = P::kStages;
   constexpr int kAccBufs = P::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
@@ -367,7 +479,6 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
   // Work units: (tile, K slice) pairs, unit u = tile * splits + slice.
-  const int units = args.tiles_m * args.tiles_n * args.splits;
 
   // 1 KiB aligned start: the 128 B swizzle atoms (8 rows x 128 B) must be.
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -425,9 +536,10 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       uint32_t stage = 0, phase = 0;
       uint32_t filled = 0;  // ring slots this producer has filled so far
       bool ok = true;
-      for (int u = pair; ok && u < units; u += npairs) {
-        int tm, tn, kb0, kb1;
-        unit_coord<kOut>(u, args, &tm, &tn, &kb0, &kb1);
+      WorkIter wi;
+      wi.init(args, pair, npairs);
+      int tm, tn, kb0, kb1, skt;
+      while (ok && wi.template next<kOut, kSK>(args, &tm, &tn, &kb0, &kb1, &skt)) {
         const int a_row = tm * kPairM + (int)rank * kCtaM;
         const int b_row = tn * P::kTileN + (int)rank * P::kRowsB;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -471,10 +583,12 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       uint32_t stage = 0, phase = 0;
       int it = 0;
       bool ok = true;
-      for (int u = pair; ok && u < units; u += npairs, ++it) {
-        int tm, tn, kb0, kb1;
-        unit_coord<kOut>(u, args, &tm, &tn, &kb0, &kb1);
-        const uint32_t buf = it % kAccBufs, acc_phase = (it / kAccBufs) & 1;
+      WorkIter wi;
+      wi.init(args, pair, npairs);
+      int tm, tn, kb0, kb1, skt;
+      while (ok && wi.template next<kOut, kSK>(args, &tm, &tn, &kb0, &kb1, &skt)) {
+        const int my_it = it++;
+        const uint32_t buf = my_it % kAccBufs, acc_phase = (my_it / kAccBufs) & 1;
         if constexpr (kProfile) prof.start(kTagWaitEpilogue);
         if (!wait_bounded(smem_u32(&bar_acc_empty[buf]), acc_phase ^ 1u, wctx, kErrWaitAccEmpty))
           break;
@@ -533,10 +647,12 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const uint32_t acc_empty_leader = cluster_map(smem_u32(&bar_acc_empty[0]), 0);
     uint32_t nstore = 0;
     int it = 0;
-    for (int u = pair; u < units; u += npairs, ++it) {
-      int tm, tn, kb0, kb1;
-      unit_coord<kOut>(u, args, &tm, &tn, &kb0, &kb1);
-      const uint32_t buf = it % kAccBufs, acc_phase = (it / kAccBufs) & 1;
+    WorkIter wi;
+    wi.init(args, pair, npairs);
+    int tm, tn, kb0, kb1, skt;
+    while (wi.template next<kOut, kSK>(args, &tm, &tn, &kb0, &kb1, &skt)) {
+      const int my_it = it++;
+      const uint32_t buf = my_it % kAccBufs, acc_phase = (my_it / kAccBufs) & 1;
       if constexpr (kProfile) {
         if (lane == 0) prof.start(kTagWaitMainloop);
       }
@@ -554,6 +670,39 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           tmem_base + buf * P::kTileN + sub * kSubW + ((uint32_t)(quarter * 32) << 16);
       const int row0 = tm * kPairM + (int)rank * kCtaM + quarter * 32;
       const int col0 = tn * P::kTileN + sub * kSubW;
+      // Stream-K tile cut between pairs: a piece that is not the tile's last
+      // K blocks goes to this pair's slot for the pair that finishes the
+      // tile; the last K blocks wait for the earlier pieces (heads) and add
+      // them while draining (sk_heads > 0).
+      int sk_heads = 0;
+      const float* sk_piece = nullptr;
+      constexpr long long kSkStride = 2LL * P::kEpiWarps * kPieceFloats;  // one pair's pieces
+      if constexpr (kSK) {
+        if (skt >= 0 && !(kb0 == 0 && kb1 == args.k_blocks)) {
+          const int piece = (int)rank * P::kEpiWarps + ew;
+          if (kb1 < args.k_blocks) {
+            const long long slot = (long long)pair * 2 * P::kEpiWarps + piece;
+            ks_send_piece<false>(tbase, args.sk_slots + slot * kPieceFloats,
+                                 args.sk_flags + slot, args.sk_epoch,
+                                 acc_empty_leader + buf * 8u);
+            if constexpr (kProfile) {
+              if (lane == 0) prof.stop();
+            }
+            continue;
+          }
+          const int c0 = sk_owner((long long)skt * args.k_blocks, args.sk_items,
+                                  sk_pairs(args, npairs));
+          bool ready = true;
+#pragma unroll 1
+          for (int c = c0; ready && c < pair; ++c)
+            ready = wait_peer_flag<false>(args.sk_flags + (long long)c * 2 * P::kEpiWarps + piece,
+                                          args.sk_epoch, wctx, args.timeout_ns, kErrWaitPartial);
+          if (!ready) break;
+          sk_heads = pair - c0;
+          sk_piece = args.sk_slots + ((long long)c0 * 2 * P::kEpiWarps + piece) * kPieceFloats +
+                     4 * lane;
+        }
+      }
       // Row `lane` of a 32x64 box is 8 chunks of 16 B; chunk j is stored at
       // position j ^ (row % 8) -- the TMA 128 B swizzle pattern.
       const uint32_t row_off = lane * 128u;
@@ -632,6 +781,12 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           if constexpr (kOut == kOutKsplit) {
             ks_accumulate(v0, recv, recv_stride, 2 * c, args.ks.rank, args.ks.nranks);
             ks_accumulate(v1, recv, recv_stride, 2 * c + 1, args.ks.rank, args.ks.nranks);
+          }
+          if constexpr (kSK) {
+            if (sk_heads > 0) {
+              sk_accumulate(v0, sk_piece, kSkStride, sk_heads, 2 * c);
+              sk_accumulate(v1, sk_piece, kSkStride, sk_heads, 2 * c + 1);
+            }
           }
           if (c == kSubW / kStoreCols - 1) {
             // All of this warp's part of the buffer is in registers: hand

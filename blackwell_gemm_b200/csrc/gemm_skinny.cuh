@@ -490,16 +490,6 @@ struct SkinnyStreamArgs {
   unsigned long long timeout_ns;
 };
 
-__device__ __forceinline__ unsigned int ld_acquire_gpu_u32(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release_gpu_u32(unsigned int* p, unsigned int v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
 // First CTA (of G) whose range [c total / G, (c+1) total / G) holds item x.
 __device__ __forceinline__ int stream_owner(long long x, long long total, int G) {
   return (int)(((x + 1) * G + total - 1) / total) - 1;

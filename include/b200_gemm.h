@@ -99,6 +99,17 @@ int b200_gemm_get_splits(int M, int N, int K, int* splits);
  * the mode.  No reference counterpart. */
 int b200_gemm_set_skinny_mode(int mode);
 
+/* Stream-K tail of the 256 x 256 pair-tile kernels: when the tiles are more than
+ * one wave of the persistent grid but not a whole number of waves, the whole
+ * waves run as usual and the remaining tiles' (tile, K block) items are split
+ * evenly over all pairs; a tile cut between pairs is summed in the kernel by
+ * the pair holding its last K blocks (fp32 pieces through a pool workspace,
+ * one rounding).  0 = off, 1 = when the last wave would idle at least 3 % of
+ * the pair-slots (default; B200_GEMM_STREAMK overrides), 2 = whenever the
+ * last wave is partial.  No reference counterpart (the reference deals whole
+ * tiles with cluster launch control). */
+int b200_gemm_set_stream_k(int mode);
+
 /* Same GEMM with the intra-kernel profiler on (never split).  `profiler` is a device int64
  * buffer of rows x (1 + 4 * num_entries) entries, rows from
  * b200_gemm_profile_rows; row r = block * warps_per_cta + warp (warps per
