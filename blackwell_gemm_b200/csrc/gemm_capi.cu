@@ -587,8 +587,8 @@ int launch_streamk(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
 template <bool kProfile>
 int launch_bf16(int v, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                 const void* B, int ldb, const GemmArgs& args, const DeviceState& d,
-                cudaStream_t stream) {
-  if (!kProfile && (v == kV256x64 || v == kV256x128)) {
+                cudaStream_t stream, bool may_allocate = true) {
+  if (!kProfile && may_allocate && (v == kV256x64 || v == kV256x128)) {
     bool used = false;
     const int st = v == kV256x128 ? launch_streamk<kV256x128>(ta, tb, tc, args, d, stream, &used)
                                   : launch_streamk<kV256x64>(ta, tb, tc, args, d, stream, &used);
@@ -1666,8 +1666,9 @@ int run_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K,
     return cast_to_bf16(W, ldw, C, ldc, M, N, nd->launch.sms, stream);
   }
   if (encode_2d(&tc, C, N, M, ldc, kStoreCols, 32) != B200_OK) return B200_ERR_TENSOR_MAP;
+  // (no stream-K tail here: its workspace and flags would be allocations)
   return launch_bf16<false>(choose_variant(M, N, nd->launch.max_pairs), ta, tb, tc, B, ldb, args,
-                            nd->launch, stream);
+                            nd->launch, stream, false);
 }
 
 }  // namespace

@@ -47,10 +47,21 @@ def test_exact_inputs_bit_exact(M, N, K, block_rows):
 def test_random_matches_device_gemm(pinned):
     M, N, K = 3000, 2048, 2048
     A, Bt = workloads.make_operands(M, N, K, seed=5)
-    C = host_gemm(A.cpu(), Bt.cpu(), 512, pinned)
+    capi.set_stream_k(0)
+    try:
+        C = host_gemm(A.cpu(), Bt.cpu(), 512, pinned)
+    finally:
+        capi.set_stream_k(1)
     ref = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-    assert capi.gemm_bf16(A.data_ptr(), Bt.data_ptr(), ref.data_ptr(), M, N, K, K, K, N, 0) == capi.OK
-    torch.cuda.synchronize()
+    # whole-tile kernels on both sides (a stream-K tail sums split tiles in
+    # another grouping), so the bits must agree
+    capi.set_stream_k(0)
+    try:
+        assert capi.gemm_bf16(A.data_ptr(), Bt.data_ptr(), ref.data_ptr(), M, N, K, K, K, N,
+                              0) == capi.OK
+        torch.cuda.synchronize()
+    finally:
+        capi.set_stream_k(1)
     assert torch.equal(C.view(torch.int16), ref.cpu().view(torch.int16))
     assert parity.passes(parity.metrics(C.cuda(), A.float() @ Bt.float().T, A, Bt))
 

@@ -15,7 +15,8 @@ pytestmark = pytest.mark.gpu
 SHAPES = [(256, 2048, 8192),     # split-K through the fixed workspace
           (16, 8192, 8192),      # skinny
           (1024, 1024, 1024),    # not split: only the error word is used
-          (300, 520, 4096)]      # ragged
+          (300, 520, 4096),      # ragged
+          (4096, 4096, 1024)]    # the allocating path would add a stream-K tail
 
 
 def run(fn, A, Bt, C):
