@@ -89,7 +89,10 @@ def pci_bus_string(device: int) -> str:
 
 
 class ClockSampler:
-    """Samples SM clock and clock-event reasons of one GPU through NVML."""
+    """Samples SM clock and clock-event reasons of one GPU through NVML every
+    `period_s`, from a thread, between start() and stop().  The NVML calls are
+    made once in the constructor so the first timed sample is not slowed by
+    library set-up."""
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
@@ -104,18 +107,23 @@ class ClockSampler:
             self.h = pynvml.nvmlDeviceGetHandleByPciBusId(pci_bus_string(device).encode())
             self.nv = pynvml
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            pynvml.nvmlDeviceGetClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
         except Exception as e:  # NVML missing: report it, do not fail the bench
             self.nv, self.err = None, repr(e)
+
+    def _sample(self):
+        self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+        self.reasons |= int(self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
 
     def _run(self):
         while not self._stop.is_set():
             try:
-                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
-                self.reasons |= int(self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+                self._sample()
             except Exception as e:
                 self.err = repr(e)
                 return
-            time.sleep(self.period)
+            self._stop.wait(self.period)
 
     def start(self):
         if self.nv:
@@ -126,6 +134,11 @@ class ClockSampler:
         if self._th:
             self._stop.set()
             self._th.join()
+            if not self.samples:
+                try:  # the region ended before the thread ran: one sample now
+                    self._sample()
+                except Exception as e:
+                    self.err = repr(e)
 
     def report(self):
         names = [n for b, n in self.REASONS.items() if self.reasons & b]

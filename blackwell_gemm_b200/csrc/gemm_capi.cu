@@ -223,23 +223,29 @@ int init_variants(int sms, int* max_pairs) {
   return B200_OK;
 }
 
+// 128-row blocks of B per unit of the persistent skinny kernel: two while
+// two accumulators of 2 x Mp columns fit in TMEM.
+constexpr int skinny_tiles(int mp) { return mp >= 256 ? 1 : 2; }
+
+// kSlabs: K slabs per stage asked for; each kernel gets the most that fit.
 template <int kMp, int kSlabs>
 bool set_skinny_limit() {
-  return cudaFuncSetAttribute(gemm_skinny_kernel<kMp, kSlabs>,
+  constexpr int kT = skinny_tiles(kMp);
+  constexpr int kSp = skinny_fit_slabs(kMp, kSlabs, kT);
+  constexpr int kSs = skinny_fit_slabs(kMp, kSlabs);
+  return cudaFuncSetAttribute(gemm_skinny_kernel<kMp, kSp, kT>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              SkinnyCfg<kMp, kSlabs>::kSmemBytes) == cudaSuccess &&
-         cudaFuncSetAttribute(gemm_skinny_stream_kernel<kMp, kSlabs>,
+                              SkinnyCfg<kMp, kSp, kT>::kSmemBytes) == cudaSuccess &&
+         cudaFuncSetAttribute(gemm_skinny_stream_kernel<kMp, kSs>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              SkinnyCfg<kMp, kSlabs>::kSmemBytes) == cudaSuccess;
+                              SkinnyCfg<kMp, kSs>::kSmemBytes) == cudaSuccess;
 }
 
 template <int kSlabs>
 bool set_skinny_limits_for() {
-  return set_skinny_limit<16, skinny_fit_slabs(16, kSlabs)>() &&
-         set_skinny_limit<32, skinny_fit_slabs(32, kSlabs)>() &&
-         set_skinny_limit<64, skinny_fit_slabs(64, kSlabs)>() &&
-         set_skinny_limit<128, skinny_fit_slabs(128, kSlabs)>() &&
-         set_skinny_limit<256, skinny_fit_slabs(256, kSlabs)>();
+  return set_skinny_limit<16, kSlabs>() && set_skinny_limit<32, kSlabs>() &&
+         set_skinny_limit<64, kSlabs>() && set_skinny_limit<128, kSlabs>() &&
+         set_skinny_limit<256, kSlabs>();
 }
 
 bool set_skinny_limits() {
@@ -644,10 +650,12 @@ int choose_skinny_splits(long long tiles, int k_blocks, int ctas, int M, int N, 
 
 constexpr int kSkinnyMaxM = 256;
 
-template <int kMp, int kSlabs>
+template <int kMp, int kSlabsWanted>
 int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
                   int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi) {
-  using P = SkinnyCfg<kMp, kSlabs>;
+  constexpr int kTiles = skinny_tiles(kMp);
+  constexpr int kSlabs = skinny_fit_slabs(kMp, kSlabsWanted, kTiles);
+  using P = SkinnyCfg<kMp, kSlabs, kTiles>;
   CUtensorMap tb, ta, tw;
   if (encode_2d(&tb, B, K, N, ldb, kSlabK, P::kRowsB) != B200_OK ||
       encode_2d(&ta, A, K, M, lda, kSlabK, kMp) != B200_OK)
@@ -658,8 +666,9 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
   args.N = N;
   args.K = K;
   args.tiles = (int)ceil_div(N, P::kRowsB);
+  args.groups = (int)ceil_div(args.tiles, kTiles);
   args.k_blocks = (int)ceil_div(K, P::kBK);
-  int splits = choose_skinny_splits(args.tiles, args.k_blocks, d.sms, M, N, K);
+  int splits = choose_skinny_splits(args.groups, args.k_blocks, d.sms, M, N, K);
   args.kb_per_split = (int)ceil_div(args.k_blocks, splits);
   args.splits = (int)ceil_div(args.k_blocks, args.kb_per_split);
   args.status = d.status;
@@ -675,10 +684,10 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
   int st = encode_2d(&tw, W, N, M, ldw, 32, P::kChunk, true, false);
   if (st == B200_OK && cudaMemsetAsync(W, 0, bytes, stream) != cudaSuccess) st = B200_ERR_LAUNCH;
   if (st == B200_OK) {
-    const long long units = (long long)args.tiles * args.splits;
+    const long long units = (long long)args.groups * args.splits;
     const int grid = (int)(units < d.sms ? units : d.sms);
-    gemm_skinny_kernel<kMp, kSlabs><<<grid, P::kThreads, P::kSmemBytes, stream>>>(tb, ta, tw,
-                                                                                args);
+    gemm_skinny_kernel<kMp, kSlabs, kTiles><<<grid, P::kThreads, P::kSmemBytes, stream>>>(
+        tb, ta, tw, args);
     if (cudaGetLastError() != cudaSuccess) st = B200_ERR_LAUNCH;
   }
   if (st == B200_OK) st = cast_to_bf16(W, ldw, C, ldc, M, N, d.sms, stream, epi);
@@ -758,19 +767,14 @@ template <int kSlabs>
 int run_skinny_slabs(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
                      int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi) {
   if (M <= 16)
-    return launch_skinny<16, skinny_fit_slabs(16, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
-                                                            stream, epi);
+    return launch_skinny<16, kSlabs>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
   if (M <= 32)
-    return launch_skinny<32, skinny_fit_slabs(32, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
-                                                            stream, epi);
+    return launch_skinny<32, kSlabs>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
   if (M <= 64)
-    return launch_skinny<64, skinny_fit_slabs(64, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
-                                                            stream, epi);
+    return launch_skinny<64, kSlabs>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
   if (M <= 128)
-    return launch_skinny<128, skinny_fit_slabs(128, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
-                                                              stream, epi);
-  return launch_skinny<256, skinny_fit_slabs(256, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d,
-                                                            stream, epi);
+    return launch_skinny<128, kSlabs>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
+  return launch_skinny<256, kSlabs>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
 }
 
 // K slabs per stage of the skinny kernel (B200_GEMM_SKINNY_SLABS: 1, 2, 4).
@@ -862,7 +866,10 @@ int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int l
   // better.  B200_GEMM_SKINNY=2 forces the cluster kernel for every M,
   // 3 the stream-K kernel.
   const int mode = skinny_mode();
-  if (epi == nullptr && mode == 3) {
+  // Stream-K for 16 < M <= 64 (measured 1-3 us ahead of the persistent
+  // kernel at N = K = 8192, where the workspace clear and rounding pass weigh
+  // most); the persistent kernel above.
+  if (epi == nullptr && (mode == 3 || (mode == 1 && M > 16 && M <= 64))) {
     switch (skinny_slabs()) {
       case 1: return run_skinny_stream_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
       case 4: return run_skinny_stream_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
@@ -909,8 +916,22 @@ int skinny_slices(int M, int N, int K, const DeviceState* d) {
     return 1;
   }
   const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-  const int k_blocks = (int)ceil_div(K, skinny_fit_slabs(mp, skinny_slabs()) * kSlabK);
-  const int s = choose_skinny_splits(tiles, k_blocks, d ? d->sms : 148, M, N, K);
+  if (mode == 3 || (mode == 1 && M > 16 && M <= 64)) {
+    // stream-K: the most CTAs any one block of B is cut between
+    const long long kb = ceil_div(K, skinny_fit_slabs(mp, skinny_slabs()) * kSlabK);
+    const long long total = tiles * kb;
+    const int G = (int)(total < (d ? d->sms : 148) ? total : (d ? d->sms : 148));
+    long long most = 1;
+    for (long long t = 0; t < tiles; ++t) {
+      const long long c = stream_owner_host(t * kb + kb - 1, total, G) -
+                          stream_owner_host(t * kb, total, G) + 1;
+      if (c > most) most = c;
+    }
+    return (int)most;
+  }
+  const int nt = skinny_tiles(mp);
+  const int k_blocks = (int)ceil_div(K, skinny_fit_slabs(mp, skinny_slabs(), nt) * kSlabK);
+  const int s = choose_skinny_splits(ceil_div(tiles, nt), k_blocks, d ? d->sms : 148, M, N, K);
   return (int)ceil_div(k_blocks, ceil_div(k_blocks, s));
 }
 

@@ -34,14 +34,19 @@ __device__ __forceinline__ int skinny_kb(int kb0, int len, int i, int t, int T) 
   return kb0 + j;
 }
 
-template <int kMp, int kSlabs>
+// kTiles: 128-row blocks of B per work unit.  Every CTA streams its own rows
+// of B but re-reads A's slab for each unit, and each SM's inflow is the
+// limit in this HBM-bound regime, so a unit of kTiles blocks sharing one A
+// slab per K step cuts A's share of the inflow kTiles-fold.
+template <int kMp, int kSlabs, int kTiles = 1>
 struct SkinnyCfg {
   static_assert(kMp % 16 == 0 && kMp >= 16 && kMp <= 256, "MMA N must be 16..256, step 16");
-  static constexpr int kRowsB = 128;                       // MMA M: rows of B per unit
+  static_assert(2 * kTiles * kMp <= 512, "two accumulators of kTiles x Mp columns exceed TMEM");
+  static constexpr int kRowsB = 128;                       // MMA M: rows of B per block
   static constexpr int kBK = kSlabs * kSlabK;              // K per stage
   static constexpr int kSlabB = kRowsB * kSlabK * 2;       // 16 KiB
   static constexpr int kSlabA = kMp * kSlabK * 2;
-  static constexpr int kBytesB = kSlabs * kSlabB;
+  static constexpr int kBytesB = kTiles * kSlabs * kSlabB;
   static constexpr int kBytesA = kSlabs * kSlabA;
   static constexpr int kStageBytes = kBytesB + kBytesA;
   static constexpr int kChunk = kMp < 32 ? kMp : 32;       // epilogue columns per pass
@@ -50,17 +55,22 @@ struct SkinnyCfg {
   static constexpr int kStagesFit = (kSmemBudget - kStoreBytes - kSmemReserve) / kStageBytes;
   static constexpr int kStages = kStagesFit > 16 ? 16 : kStagesFit;
   static constexpr int kSmemBytes = kStages * kStageBytes + kStoreBytes + 1024;
-  static constexpr int kTmemAlloc = 2 * kMp <= 32 ? 32 : 2 * kMp;  // power of two >= 32
+  static constexpr int kTmemCols = 2 * kTiles * kMp;     // two accumulators
+  static constexpr int kTmemAlloc = kTmemCols <= 32    ? 32
+                                    : kTmemCols <= 64  ? 64
+                                    : kTmemCols <= 128 ? 128
+                                    : kTmemCols <= 256 ? 256
+                                                       : 512;  // power of two >= 32
   static constexpr int kThreads = 192;
   static_assert(kStages >= 2, "ring too shallow");
 };
 
 // Largest K-slab count <= `want` whose stages still leave a ring of three.
-constexpr int skinny_fit_slabs(int mp, int want) {
+constexpr int skinny_fit_slabs(int mp, int want, int tiles = 1) {
   for (int s = want; s > 1; --s) {
     const int chunk = mp < 32 ? mp : 32;
     const int store = 4 * 2 * 32 * chunk * 4;
-    const int stage = s * (128 * kSlabK * 2 + mp * kSlabK * 2);
+    const int stage = s * (tiles * 128 * kSlabK * 2 + mp * kSlabK * 2);
     if ((kSmemBudget - store - kSmemReserve) / stage >= 3) return s;
   }
   return 1;
@@ -70,20 +80,21 @@ struct SkinnyArgs {
   int M, N, K;
   int l2_hint;       // 1: B loads evict-first, A loads evict-last in L2
   int tiles;         // ceil(N / 128)
+  int groups;        // ceil(tiles / kTiles): the units' blocks of B
   int k_blocks;      // ceil(K / kBK)
-  int splits;        // K slices per tile
+  int splits;        // K slices per group
   int kb_per_split;
   int* status;
   unsigned long long timeout_ns;
 };
 
-template <int kMp, int kSlabs>
+template <int kMp, int kSlabs, int kTiles>
 __global__ void __launch_bounds__(192, 1)
 gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 64 x 128
                    const __grid_constant__ CUtensorMap tmap_a,   // M x K, box 64 x Mp
                    const __grid_constant__ CUtensorMap tmap_w,   // W fp32 M x N, box 32 x kChunk
                    const SkinnyArgs args) {
-  using P = SkinnyCfg<kMp, kSlabs>;
+  using P = SkinnyCfg<kMp, kSlabs, kTiles>;
   constexpr int kStages = P::kStages;
   extern __shared__ uint8_t smem_raw[];
   __shared__ alignas(8) uint64_t bar_full[kStages];
@@ -96,7 +107,7 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int units = args.tiles * args.splits;
+  const int units = args.groups * args.splits;
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t store_base = smem_base + kStages * P::kStageBytes;
 
@@ -149,7 +160,7 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
         int tile, kb0, kb1;
         unit_range(u, &tile, &kb0, &kb1);
         for (int i = 0; i < kb1 - kb0; ++i) {
-          const int kb = skinny_kb(kb0, kb1 - kb0, i, tile, args.tiles);
+          const int kb = skinny_kb(kb0, kb1 - kb0, i, tile, args.groups);
           if (!wait_bounded(smem_u32(&bar_empty[stage]), phase ^ 1u, wctx, kErrWaitEmpty)) {
             ok = false;
             break;
@@ -161,8 +172,11 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
           // segments are requested together.
 #pragma unroll
           for (int sl = 0; sl < kSlabs; ++sl)
-            tma_load_2d_hint(sb + sl * P::kSlabB, &tmap_b, kb * P::kBK + sl * kSlabK,
-                             tile * P::kRowsB, fb, pol_b);
+#pragma unroll
+            for (int b = 0; b < kTiles; ++b)
+              tma_load_2d_hint(sb + (b * kSlabs + sl) * P::kSlabB, &tmap_b,
+                               kb * P::kBK + sl * kSlabK, (tile * kTiles + b) * P::kRowsB, fb,
+                               pol_b);
 #pragma unroll
           for (int sl = 0; sl < kSlabs; ++sl)
             tma_load_2d_hint(sb + P::kBytesB + sl * P::kSlabA, &tmap_a, kb * P::kBK + sl * kSlabK,
@@ -185,7 +199,7 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
         if (!wait_bounded(smem_u32(&bar_acc_empty[buf]), acc_phase ^ 1u, wctx, kErrWaitAccEmpty))
           break;
         tc_fence_after_sync();
-        const uint32_t d_tmem = tmem_base + buf * kMp;
+        const uint32_t d_tmem = tmem_base + buf * kTiles * kMp;
         for (int kb = kb0; kb < kb1; ++kb) {  // slabs arrive in the producer's order
           if (!wait_bounded(smem_u32(&bar_full[stage]), phase, wctx, kErrWaitFull)) {
             ok = false;
@@ -195,12 +209,15 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
           const uint32_t sb = smem_base + stage * P::kStageBytes;
 #pragma unroll
           for (int sl = 0; sl < kSlabs; ++sl) {
-            const uint64_t bdesc_big = make_sdesc_k128(sb + sl * P::kSlabB);
             const uint64_t adesc_small = make_sdesc_k128(sb + P::kBytesB + sl * P::kSlabA);
 #pragma unroll
-            for (int k = 0; k < kSlabK / kMmaK; ++k)
-              umma_bf16_1(d_tmem, bdesc_big + 2ull * k, adesc_small + 2ull * k, idesc,
-                          (kb != kb0 || sl != 0 || k != 0) ? 1u : 0u);
+            for (int b = 0; b < kTiles; ++b) {
+              const uint64_t bdesc_big = make_sdesc_k128(sb + (b * kSlabs + sl) * P::kSlabB);
+#pragma unroll
+              for (int k = 0; k < kSlabK / kMmaK; ++k)
+                umma_bf16_1(d_tmem + b * kMp, bdesc_big + 2ull * k, adesc_small + 2ull * k, idesc,
+                            (kb != kb0 || sl != 0 || k != 0) ? 1u : 0u);
+            }
           }
           umma_commit_1(smem_u32(&bar_empty[stage]));
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
@@ -228,10 +245,15 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after_sync();
-      const uint32_t tbase = tmem_base + buf * kMp + ((uint32_t)(quarter * 32) << 16);
-      const int n0 = tile * P::kRowsB + quarter * 32;
+      // Block b of the unit: TMEM columns b Mp .. b Mp + Mp - 1 of buffer buf.
+      constexpr int kChunks = kTiles * (kMp / P::kChunk);
 #pragma unroll 1
-      for (int c = 0; c < kMp / P::kChunk; ++c) {
+      for (int cb = 0; cb < kChunks; ++cb) {
+        const int b = cb / (kMp / P::kChunk);
+        const int c = cb - b * (kMp / P::kChunk);
+        const uint32_t tbase =
+            tmem_base + (buf * kTiles + b) * kMp + ((uint32_t)(quarter * 32) << 16);
+        const int n0 = (tile * kTiles + b) * P::kRowsB + quarter * 32;
         uint32_t v[P::kChunk];
         if constexpr (P::kChunk == 16) {
           tmem_ld_32x32b_x16(tbase + c * 16, *reinterpret_cast<uint32_t(*)[16]>(v));
@@ -239,11 +261,12 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
           tmem_ld_32x32b_x32(tbase + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v));
         }
         tmem_wait_ld();
-        if (c == kMp / P::kChunk - 1) {
+        if (cb == kChunks - 1) {
           tc_fence_before_sync();
           __syncwarp();
           if (lane == 0) mbar_arrive_local(smem_u32(&bar_acc_empty[buf]));
         }
+        if (n0 >= args.N) continue;  // a block of the last unit past N (B read as zeros)
         const uint32_t sb = my_store + (nstore & 1u) * P::kStoreBuf;
         if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
