@@ -223,9 +223,10 @@ int init_variants(int sms, int* max_pairs) {
   return B200_OK;
 }
 
-// 128-row blocks of B per unit of the persistent skinny kernel: two while
-// two accumulators of 2 x Mp columns fit in TMEM.
-constexpr int skinny_tiles(int mp) { return mp >= 256 ? 1 : 2; }
+// 128-row blocks of B per unit of the persistent skinny kernel: two (for Mp =
+// 256 with a single accumulator, as two no longer fit in TMEM).  Four blocks
+// per unit were measured slower at Mp = 128: the ring shrinks to two stages.
+constexpr int skinny_tiles(int mp) { return mp > 0 ? 2 : 1; }
 
 // kSlabs: K slabs per stage asked for; each kernel gets the most that fit.
 template <int kMp, int kSlabs>

@@ -41,7 +41,10 @@ __device__ __forceinline__ int skinny_kb(int kb0, int len, int i, int t, int T) 
 template <int kMp, int kSlabs, int kTiles = 1>
 struct SkinnyCfg {
   static_assert(kMp % 16 == 0 && kMp >= 16 && kMp <= 256, "MMA N must be 16..256, step 16");
-  static_assert(2 * kTiles * kMp <= 512, "two accumulators of kTiles x Mp columns exceed TMEM");
+  static_assert(kTiles * kMp <= 512, "an accumulator of kTiles x Mp columns exceeds TMEM");
+  // Two accumulators (the epilogue of one unit overlaps the next unit's
+  // MMAs) when they fit in TMEM's 512 columns, else one.
+  static constexpr int kAccBufs = 2 * kTiles * kMp <= 512 ? 2 : 1;
   static constexpr int kRowsB = 128;                       // MMA M: rows of B per block
   static constexpr int kBK = kSlabs * kSlabK;              // K per stage
   static constexpr int kSlabB = kRowsB * kSlabK * 2;       // 16 KiB
@@ -55,7 +58,7 @@ struct SkinnyCfg {
   static constexpr int kStagesFit = (kSmemBudget - kStoreBytes - kSmemReserve) / kStageBytes;
   static constexpr int kStages = kStagesFit > 16 ? 16 : kStagesFit;
   static constexpr int kSmemBytes = kStages * kStageBytes + kStoreBytes + 1024;
-  static constexpr int kTmemCols = 2 * kTiles * kMp;     // two accumulators
+  static constexpr int kTmemCols = kAccBufs * kTiles * kMp;
   static constexpr int kTmemAlloc = kTmemCols <= 32    ? 32
                                     : kTmemCols <= 64  ? 64
                                     : kTmemCols <= 128 ? 128
@@ -195,7 +198,7 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
       for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++it) {
         int tile, kb0, kb1;
         unit_range(u, &tile, &kb0, &kb1);
-        const uint32_t buf = it & 1, acc_phase = (it >> 1) & 1;
+        const uint32_t buf = it % P::kAccBufs, acc_phase = (it / P::kAccBufs) & 1;
         if (!wait_bounded(smem_u32(&bar_acc_empty[buf]), acc_phase ^ 1u, wctx, kErrWaitAccEmpty))
           break;
         tc_fence_after_sync();
@@ -239,7 +242,7 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
       int tile, kb0, kb1;
       unit_range(u, &tile, &kb0, &kb1);
-      const uint32_t buf = it & 1, acc_phase = (it >> 1) & 1;
+      const uint32_t buf = it % P::kAccBufs, acc_phase = (it / P::kAccBufs) & 1;
       int ok = 0;
       if (lane == 0) ok = wait_bounded(smem_u32(&bar_acc_full[buf]), acc_phase, wctx, kErrWaitAccFull);
       ok = __shfl_sync(0xffffffffu, ok, 0);
