@@ -328,10 +328,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip e2e, baselines and the CPU sample (timing only)")
-    ap.add_argument("--mode", choices=["rows", "ksplit"], default="rows",
+    ap.add_argument("--mode", choices=["rows", "ksplit", "sweep"], default="rows",
                     help="rows: 8192^3 per GPU, rows of A sharded (default, the headline); "
                          "ksplit: 8192 x 8192 x 131072 with K split across the GPUs, "
-                         "fp32 partials summed by an NCCL reduce-scatter")
+                         "reduced inside the GEMM kernel over NVLink; "
+                         "sweep: every single-GPU configuration shape, one line each")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -347,6 +348,8 @@ def main():
         return run_reference(args, world, rank, dev)
     if args.mode == "ksplit":
         return run_ksplit(args, world, rank, dev)
+    if args.mode == "sweep":
+        return run_sweep(args, world, rank, dev)
 
     import torch.distributed as dist
     if world > 1:
@@ -587,6 +590,61 @@ def run_ksplit(args, world, rank, dev):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_sweep(args, world, rank, dev):
+    """Every single-GPU configuration shape (workloads.CONFIGS: 1024^3, the
+    square sweep, the transformer projections, the skinny decode shapes), one
+    JSON line each on rank 0: cold-L2 medians of ours, cuBLAS and the
+    reference's v8 (where it supports the shape) in the same process, the
+    roofline fraction (tensor peak, or HBM for the skinny shapes) and parity on
+    sampled rows.  Not the driver's bench line; the evidence for the configs."""
+    if rank != 0:
+        return
+    import oracle
+    from blackwell_gemm_b200 import workloads
+    from blackwell_gemm_b200.workloads import CONFIGS, WEIGHT_STD, make_operands
+    peaks, src = measured_peaks()
+    peak_tf = float(peaks.get("bf16_tflops", FALLBACK_BF16_TFLOPS))
+    peak_gbs = float(peaks.get("hbm_gbs", 6650.0))
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    steps = max(10, min(args.steps, 50))
+    for name in ("square_1024", "square", "projection", "skinny"):
+        for (M, N, K) in CONFIGS[name]:
+            A, Bt = make_operands(M, N, K, seed=M + N + K, weight_std=WEIGHT_STD[name], device=dev)
+            C = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            gemm_ours(A, Bt, C, stream)
+            torch.cuda.synchronize()
+            par = parity_sample(C, A, Bt)
+            med = lambda fn: statistics.median(time_cold(fn, steps, args.warmup, stream, flush))
+            ours = med(lambda: gemm_ours(A, Bt, C, stream))
+            cub = med(lambda: torch.matmul(A, Bt.T))
+            ref = None
+            try:
+                if oracle.ref_supports("v8", M, N, K):
+                    Cr = torch.empty_like(C)
+                    ref = med(lambda: gemm_reference(A, Bt, Cr, stream))
+            except Exception:
+                ref = None
+            fl = workloads.flops(M, N, K)
+            by = workloads.min_bytes(M, N, K)
+            tf = lambda ms: fl / (ms * 1e-3) / 1e12
+            hbm = name == "skinny"
+            achieved = by / (ours * 1e-3) / 1e9 if hbm else tf(ours)
+            print(json.dumps({
+                "config": name, "M": M, "N": N, "K": K, "ours_us": ours * 1e3,
+                "ours_tflops": tf(ours), "cublas_tflops": tf(cub),
+                "reference_v8_tflops": tf(ref) if ref else None,
+                "ours_vs_cublas": cub / ours, "ours_vs_reference": (ref / ours) if ref else None,
+                "roofline": {"bound": "hbm" if hbm else "tensor", "achieved": achieved,
+                             "peak": peak_gbs if hbm else peak_tf,
+                             "unit": "GB/s" if hbm else "TFLOP/s",
+                             "frac": achieved / (peak_gbs if hbm else peak_tf),
+                             "peak_source": src},
+                "parity": par, "timing": f"median of {steps} cold-L2 launches (256 MB flush "
+                                          "between), same process, 1 s idle before each arm",
+            }), flush=True)
 
 
 def run_reference(args, world, rank, dev):
