@@ -651,6 +651,13 @@ int choose_skinny_splits(long long tiles, int k_blocks, int ctas, int M, int N, 
 
 constexpr int kSkinnyMaxM = 256;
 
+// Rows of A up to which the cluster kernel is chosen: 8, or 16 while B is
+// under 32 M elements (measured crossovers against the stream-K kernel at
+// N = K = 4096 and 8192).
+bool skinny_use_cluster(int M, int N, int K) {
+  return M <= 8 || (M <= 16 && (long long)N * K < (32LL << 20));
+}
+
 template <int kMp, int kSlabsWanted>
 int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
                   int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi) {
@@ -739,9 +746,25 @@ int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, in
     cudaGetLastError();
     return B200_ERR_LAUNCH;
   }
-  args.flags = reinterpret_cast<unsigned int*>(ws);
   args.slots = reinterpret_cast<float*>(ws + flag_bytes);
-  int st = cudaMemsetAsync(ws, 0, flag_bytes, stream) == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
+  // Flags: the stream's epoch-numbered array outside capture (no clearing
+  // operation before the kernel), cleared workspace flags under capture.
+  int st = B200_OK;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+    cudaGetLastError();
+    cap = cudaStreamCaptureStatusActive;
+  }
+  unsigned int* persistent = nullptr;
+  if (cap == cudaStreamCaptureStatusNone)
+    persistent = stream_flags(stream, (size_t)args.tiles * max_seg * 4, &args.epoch);
+  if (persistent != nullptr) {
+    args.flags = persistent;
+  } else {
+    args.flags = reinterpret_cast<unsigned int*>(ws);
+    args.epoch = 1;
+    if (cudaMemsetAsync(ws, 0, flag_bytes, stream) != cudaSuccess) st = B200_ERR_LAUNCH;
+  }
   if (st == B200_OK) {
     gemm_skinny_stream_kernel<kMp, kSlabs><<<G, P::kThreads, P::kSmemBytes, stream>>>(tb, ta, tc,
                                                                                     args);
@@ -862,15 +885,15 @@ int run_skinny_cluster(const void* A, const void* B, void* C, int M, int N, int 
 
 int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
                int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi = nullptr) {
-  // Up to 16 rows of A the single-launch cluster kernel is faster (no
-  // workspace clear or rounding pass); above, the persistent kernel streams
-  // better.  B200_GEMM_SKINNY=2 forces the cluster kernel for every M,
-  // 3 the stream-K kernel.
+  // Per shape (mode 1): for the fewest rows of A (skinny_use_cluster) the
+  // single-launch cluster kernel (A's box is then mostly out of bounds, so
+  // nearly only B streams); up to 64 rows the stream-K kernel (all SMs, no
+  // workspace clear or rounding pass); above, the persistent split-K kernel.
+  // B200_GEMM_SKINNY=2 forces the cluster kernel for every M, 3 the
+  // stream-K kernel.
   const int mode = skinny_mode();
-  // Stream-K for 16 < M <= 64 (measured 1-3 us ahead of the persistent
-  // kernel at N = K = 8192, where the workspace clear and rounding pass weigh
-  // most); the persistent kernel above.
-  if (epi == nullptr && (mode == 3 || (mode == 1 && M > 16 && M <= 64))) {
+  if (epi == nullptr &&
+      (mode == 3 || (mode == 1 && !skinny_use_cluster(M, N, K) && M <= 64))) {
     switch (skinny_slabs()) {
       case 1: return run_skinny_stream_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
       case 4: return run_skinny_stream_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
@@ -879,7 +902,7 @@ int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int l
   }
   // (The cluster kernel writes C directly, so fused epilogues take the
   // workspace kernel, whose rounding pass applies them.)
-  if (epi == nullptr && (mode == 2 || M <= 16))
+  if (epi == nullptr && (mode == 2 || skinny_use_cluster(M, N, K)))
     return run_skinny_cluster(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
   switch (skinny_slabs()) {
     case 1: return run_skinny_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
@@ -901,7 +924,7 @@ int skinny_slices(int M, int N, int K, const DeviceState* d) {
   const int mode = skinny_mode();
   const int forced = tuning_splits();
   const long long tiles = ceil_div(N, 128);
-  if (d && (mode == 2 || M <= 16)) {
+  if (d && (mode == 2 || (mode == 1 && skinny_use_cluster(M, N, K)))) {
     const int k_blocks = (int)ceil_div(K, kSlabK);
     if (forced > 0) {
       int ci = 0;
@@ -917,7 +940,7 @@ int skinny_slices(int M, int N, int K, const DeviceState* d) {
     return 1;
   }
   const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-  if (mode == 3 || (mode == 1 && M > 16 && M <= 64)) {
+  if (mode == 3 || (mode == 1 && !skinny_use_cluster(M, N, K) && M <= 64)) {
     // stream-K: the most CTAs any one block of B is cut between
     const long long kb = ceil_div(K, skinny_fit_slabs(mp, skinny_slabs()) * kSlabK);
     const long long total = tiles * kb;

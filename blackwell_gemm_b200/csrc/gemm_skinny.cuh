@@ -502,7 +502,8 @@ namespace b200 {
 //     the earlier contributors' flags -- raised at the ends of their ranges --
 //     adds slots 0..j in K order, rounds and stores C.
 // Waits only point to CTAs of lower index, which the hardware dispatches
-// first.  Slots and flags live in a per-call workspace; the flags start at 0.
+// first.  Slots live in a per-call workspace; flags are raised to the call's
+// epoch (the launcher's per-stream flag arrays, or cleared per-call flags).
 struct SkinnyStreamArgs {
   int M, N, K;
   int l2_hint;
@@ -511,7 +512,8 @@ struct SkinnyStreamArgs {
   long long total;   // tiles x k_blocks
   int max_seg;       // slots per tile
   float* slots;      // [tiles][max_seg][kMp][128] fp32
-  unsigned int* flags;  // [tiles][max_seg][4]
+  unsigned int* flags;  // [tiles][max_seg][4], below `epoch` at launch
+  unsigned int epoch;   // value a raised flag takes in this call
   int* status;
   unsigned long long timeout_ns;
 };
@@ -732,7 +734,8 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
           asm volatile("fence.acq_rel.gpu;" ::: "memory");
           __syncwarp();
           if (lane == 0)
-            st_release_gpu_u32(args.flags + ((long long)t * args.max_seg + j) * 4 + quarter, 1u);
+            st_release_gpu_u32(args.flags + ((long long)t * args.max_seg + j) * 4 + quarter,
+                               args.epoch);
         }
       }
       ++it;
@@ -746,7 +749,7 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
         const unsigned int* f = args.flags + (tslots + s) * 4 + quarter;
         const unsigned long long t0 = globaltimer_ns();
         for (;;) {
-          const bool up = ld_acquire_gpu_u32(f) != 0u;
+          const bool up = (int)(ld_acquire_gpu_u32(f) - args.epoch) >= 0;
           if (__all_sync(0xffffffffu, up)) break;
           int give_up = 0;
           if (lane == 0 && globaltimer_ns() - t0 > args.timeout_ns) {

@@ -216,3 +216,37 @@ def test_skinny_kernel_forced_splits_random(splits):
     A, Bt = workloads.make_operands(M, N, K, seed=splits, weight_std=0.02)
     C = bf16_gemm(A, Bt)
     assert parity.passes(parity.metrics(C, A.float() @ Bt.float().T, A, Bt))
+
+
+def test_skinny_stream_k_graph_replays_and_streams():
+    """The stream-K skinny kernel (16 < M <= 64 by default) raises per-stream
+    epoch flags outside capture and clears its own flags when captured."""
+    M, N, K = 48, 4096, 8192
+    A, Bt = workloads.make_operands(M, N, K, seed=31, weight_std=0.02)
+    ref = bf16_gemm(A, Bt).clone()
+    C = torch.zeros(M, N, dtype=torch.bfloat16, device="cuda")
+
+    def call(out, stream):
+        assert capi.gemm_bf16(A.data_ptr(), Bt.data_ptr(), out.data_ptr(), M, N, K, K, K, N,
+                              stream) == capi.OK
+
+    side = torch.cuda.Stream()
+    call(C, side.cuda_stream)
+    torch.cuda.synchronize()
+    assert torch.equal(C.view(torch.int16), ref.view(torch.int16))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        call(C, torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        C.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(C.view(torch.int16), ref.view(torch.int16))
+    outs = [torch.zeros_like(C) for _ in range(2)]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for _ in range(3):
+        for s, out in zip(streams, outs):
+            call(out, s.cuda_stream)
+    torch.cuda.synchronize()
+    for out in outs:
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
