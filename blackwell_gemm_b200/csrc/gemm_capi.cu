@@ -317,13 +317,14 @@ int init_device(DeviceState& d, int dev) {
     return B200_ERR_LAUNCH;
   // Split-K workspaces come from a pool of our own, allocated and freed in
   // stream order, so concurrent calls on different streams never share one;
-  // the pool keeps up to 256 MiB mapped between calls.
+  // the pool keeps up to 512 MiB mapped between calls (the host-operand
+  // entry point holds A, B and C blocks at once).
   cudaMemPoolProps props = {};
   props.allocType = cudaMemAllocationTypePinned;
   props.location.type = cudaMemLocationTypeDevice;
   props.location.id = dev;
   if (cudaMemPoolCreate(&d.pool, &props) != cudaSuccess) return B200_ERR_LAUNCH;
-  unsigned long long keep = 256ull << 20;
+  unsigned long long keep = 512ull << 20;
   if (cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep) != cudaSuccess)
     return B200_ERR_LAUNCH;
   return B200_OK;
@@ -1070,13 +1071,15 @@ int run_gemm_f32out(const void* A, const void* B, float* C, int M, int N, int K,
 }
 
 // ---------------------------------------------------------------------------
-// Host-resident operands: B goes to the device once, A streams in blocks of
-// rows.  Block i's upload, GEMM and the download of its rows of C run on three
-// streams of their own, so uploads, GEMMs and downloads of different blocks
-// overlap (the link carries data in both directions at once).  Three device
-// buffers per operand block rotate; events order buffer reuse.  The whole
-// pipeline is ordered after the caller's stream at entry and the caller's
-// stream waits for its end, so the call is asynchronous like the others.
+// Host-resident operands.  A and B go up in blocks of rows, alternately
+// (A_0, B_0, A_1, B_1, ...), into full device copies; the GEMM of C block
+// (i, j) = A_i B_j^T goes out as soon as both blocks are up, and that block of
+// C comes back as soon as it is done.  Uploads, GEMMs and downloads run on
+// three streams of their own (events order them and the reuse of four
+// rotating C buffers), so the link carries data both ways from the first
+// blocks on and the GEMMs hide under the transfers.  The pipeline is ordered
+// after the caller's stream at entry and the caller's stream waits for its
+// end, so the call is asynchronous like the others.
 struct HostPipe {
   bool ready = false;
   cudaStream_t up = nullptr, mm = nullptr, down = nullptr;
@@ -1117,21 +1120,22 @@ int run_gemm_host(const void* A, const void* B, void* C, int M, int N, int K, in
   st = host_pipe(&p);
   if (st != B200_OK) return st;
   if (block_rows == 0) {
-    block_rows = (int)(ceil_div(ceil_div(M, 8), kPairM) * kPairM);
-    if (block_rows < kPairM) block_rows = kPairM;
+    const int big = M > N ? M : N;
+    block_rows = (int)(ceil_div(ceil_div(big, 4), kPairM) * kPairM);
   }
-  if (block_rows > M) block_rows = M;
-  const int blocks = (int)ceil_div(M, block_rows);
-  constexpr int kBufs = 3;
-  const int nb = blocks < kBufs ? blocks : kBufs;
+  const int br = block_rows < M ? block_rows : M;                      // rows of A per block
+  const int bc = (int)(ceil_div(block_rows < N ? block_rows : N, 8) * 8);  // rows of B per block
+  const int mb = (int)ceil_div(M, br), nb = (int)ceil_div(N, bc);
+  const int pairs = mb * nb;
+  constexpr int kCBufs = 4;
+  const int ncb = pairs < kCBufs ? pairs : kCBufs;
   const int kd = (int)ceil_div(K > 0 ? K : 1, 8) * 8;  // device row strides: 16-byte multiples
-  const int nd = (int)ceil_div(N, 8) * 8;
-  const size_t b_bytes = (size_t)N * kd * 2;
-  const size_t a_bytes = (size_t)block_rows * kd * 2;
-  const size_t c_bytes = (size_t)block_rows * nd * 2;
-  const size_t total = b_bytes + nb * (a_bytes + c_bytes);
+  const int cld = (int)ceil_div(bc, 8) * 8;
+  const size_t a_bytes = (size_t)M * kd * 2, b_bytes = (size_t)N * kd * 2;
+  const size_t c_bytes = (size_t)br * cld * 2;
+  const size_t total = a_bytes + b_bytes + ncb * c_bytes;
 
-  const int nev = 2 + 3 * blocks;
+  const int nev = 2 + mb + nb + 2 * pairs;
   cudaEvent_t* ev = new cudaEvent_t[nev];
   int made = 0;
   for (; made < nev; ++made)
@@ -1144,9 +1148,10 @@ int run_gemm_host(const void* A, const void* B, void* C, int M, int N, int K, in
   };
   if (made < nev) return finish(B200_ERR_LAUNCH);
   cudaEvent_t ev_start = ev[0], ev_end = ev[1];
-  cudaEvent_t* ev_up = ev + 2;               // block i uploaded
-  cudaEvent_t* ev_mm = ev + 2 + blocks;      // block i's GEMM done
-  cudaEvent_t* ev_down = ev + 2 + 2 * blocks;  // block i's rows of C downloaded
+  cudaEvent_t* ev_a = ev + 2;                 // A block i uploaded
+  cudaEvent_t* ev_b = ev_a + mb;              // B block j uploaded
+  cudaEvent_t* ev_mm = ev_b + nb;             // GEMM q done
+  cudaEvent_t* ev_down = ev_mm + pairs;       // C block q downloaded
 
   bool ok = cudaEventRecord(ev_start, stream) == cudaSuccess &&
             cudaStreamWaitEvent(p->up, ev_start, 0) == cudaSuccess &&
@@ -1156,43 +1161,61 @@ int run_gemm_host(const void* A, const void* B, void* C, int M, int N, int K, in
   if (ok) ok = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), total, d->pool, p->up) ==
                cudaSuccess;
   if (!ok) return finish(B200_ERR_LAUNCH);
-  char* dB = ws;
-  char* dA = ws + b_bytes;
-  char* dC = dA + nb * a_bytes;
-  if (K > 0)
-    ok = cudaMemcpy2DAsync(dB, (size_t)kd * 2, B, (size_t)ldb * 2, (size_t)K * 2, N,
-                           cudaMemcpyHostToDevice, p->up) == cudaSuccess;
-  for (int i = 0; ok && i < blocks; ++i) {
-    const int r0 = i * block_rows;
-    const int rows = M - r0 < block_rows ? M - r0 : block_rows;
-    const int b = i % nb;
-    char* a = dA + b * a_bytes;
-    char* c = dC + b * c_bytes;
-    // upload A block i once the GEMM that last read this buffer is done
-    if (i >= nb) ok = cudaStreamWaitEvent(p->up, ev_mm[i - nb], 0) == cudaSuccess;
-    if (ok && K > 0)
-      ok = cudaMemcpy2DAsync(a, (size_t)kd * 2, static_cast<const char*>(A) + (size_t)r0 * lda * 2,
-                             (size_t)lda * 2, (size_t)K * 2, rows, cudaMemcpyHostToDevice,
-                             p->up) == cudaSuccess;
-    ok = ok && cudaEventRecord(ev_up[i], p->up) == cudaSuccess &&
-         cudaStreamWaitEvent(p->mm, ev_up[i], 0) == cudaSuccess;
-    // the GEMM writes C buffer b once its previous rows have been downloaded
-    if (ok && i >= nb) ok = cudaStreamWaitEvent(p->mm, ev_down[i - nb], 0) == cudaSuccess;
-    if (ok) ok = run_gemm<false>(a, dB, c, rows, N, K, kd, kd, nd, nullptr, 0, p->mm) == B200_OK;
-    ok = ok && cudaEventRecord(ev_mm[i], p->mm) == cudaSuccess &&
-         cudaStreamWaitEvent(p->down, ev_mm[i], 0) == cudaSuccess &&
-         cudaMemcpy2DAsync(static_cast<char*>(C) + (size_t)r0 * ldc * 2, (size_t)ldc * 2, c,
-                           (size_t)nd * 2, (size_t)N * 2, rows, cudaMemcpyDeviceToHost,
-                           p->down) == cudaSuccess &&
-         cudaEventRecord(ev_down[i], p->down) == cudaSuccess;
+  char* dA = ws;
+  char* dB = ws + a_bytes;
+  char* dC = dB + b_bytes;
+  int q = 0;  // GEMMs issued so far
+  // GEMM of C block (i, j) and the download of its rows and columns.
+  auto issue = [&](int i, int j) {
+    const int r0 = i * br, rows = M - r0 < br ? M - r0 : br;
+    const int c0 = j * bc, cols = N - c0 < bc ? N - c0 : bc;
+    char* cb = dC + (size_t)(q % ncb) * c_bytes;
+    bool good = cudaStreamWaitEvent(p->mm, ev_a[i], 0) == cudaSuccess &&
+                cudaStreamWaitEvent(p->mm, ev_b[j], 0) == cudaSuccess;
+    if (good && q >= ncb) good = cudaStreamWaitEvent(p->mm, ev_down[q - ncb], 0) == cudaSuccess;
+    if (good)
+      good = run_gemm<false>(dA + (size_t)r0 * kd * 2, dB + (size_t)c0 * kd * 2, cb, rows, cols, K,
+                             kd, kd, cld, nullptr, 0, p->mm) == B200_OK;
+    good = good && cudaEventRecord(ev_mm[q], p->mm) == cudaSuccess &&
+           cudaStreamWaitEvent(p->down, ev_mm[q], 0) == cudaSuccess &&
+           cudaMemcpy2DAsync(static_cast<char*>(C) + ((size_t)r0 * ldc + c0) * 2, (size_t)ldc * 2,
+                             cb, (size_t)cld * 2, (size_t)cols * 2, rows, cudaMemcpyDeviceToHost,
+                             p->down) == cudaSuccess &&
+           cudaEventRecord(ev_down[q], p->down) == cudaSuccess;
+    ++q;
+    return good;
+  };
+  // Upload A_0, B_0, A_1, B_1, ...; each GEMM goes out once its two blocks are up.
+  const int steps = mb > nb ? mb : nb;
+  for (int s2 = 0; ok && s2 < steps; ++s2) {
+    if (s2 < mb) {
+      const int r0 = s2 * br, rows = M - r0 < br ? M - r0 : br;
+      if (K > 0)
+        ok = cudaMemcpy2DAsync(dA + (size_t)r0 * kd * 2, (size_t)kd * 2,
+                               static_cast<const char*>(A) + (size_t)r0 * lda * 2,
+                               (size_t)lda * 2, (size_t)K * 2, rows, cudaMemcpyHostToDevice,
+                               p->up) == cudaSuccess;
+      ok = ok && cudaEventRecord(ev_a[s2], p->up) == cudaSuccess;
+      for (int j = 0; ok && j < s2 && j < nb; ++j) ok = issue(s2, j);
+    }
+    if (ok && s2 < nb) {
+      const int c0 = s2 * bc, cols = N - c0 < bc ? N - c0 : bc;
+      if (K > 0)
+        ok = cudaMemcpy2DAsync(dB + (size_t)c0 * kd * 2, (size_t)kd * 2,
+                               static_cast<const char*>(B) + (size_t)c0 * ldb * 2,
+                               (size_t)ldb * 2, (size_t)K * 2, cols, cudaMemcpyHostToDevice,
+                               p->up) == cudaSuccess;
+      ok = ok && cudaEventRecord(ev_b[s2], p->up) == cudaSuccess;
+      for (int i = 0; ok && i <= s2 && i < mb; ++i) ok = issue(i, s2);
+    }
   }
   // Join: the download stream follows the other two, frees the buffers and
   // releases the caller's stream.
   if (ok)
-    ok = cudaEventRecord(ev_up[blocks - 1], p->up) == cudaSuccess &&
-         cudaStreamWaitEvent(p->down, ev_up[blocks - 1], 0) == cudaSuccess &&
-         cudaEventRecord(ev_mm[blocks - 1], p->mm) == cudaSuccess &&
-         cudaStreamWaitEvent(p->down, ev_mm[blocks - 1], 0) == cudaSuccess;
+    ok = cudaEventRecord(ev_start, p->up) == cudaSuccess &&
+         cudaStreamWaitEvent(p->down, ev_start, 0) == cudaSuccess &&
+         cudaEventRecord(ev_mm[pairs - 1], p->mm) == cudaSuccess &&
+         cudaStreamWaitEvent(p->down, ev_mm[pairs - 1], 0) == cudaSuccess;
   cudaFreeAsync(ws, p->down);
   ok = ok && cudaEventRecord(ev_end, p->down) == cudaSuccess &&
        cudaStreamWaitEvent(stream, ev_end, 0) == cudaSuccess;

@@ -63,13 +63,14 @@ int b200_gemm_bf16_epilogue(const void* A, const void* B, void* C, int M, int N,
                             const void* residual, int ldr, void* stream);
 
 /* The same GEMM on operands in HOST memory (A, B and C host pointers; page-
- * locked memory lets the transfers run asynchronously and overlap).  B is
- * copied to the device once per call; A is streamed in blocks of block_rows
- * rows (0 = chosen: M / 8 rounded up to 256); each block's upload, GEMM and
- * the download of its rows of C run on three internal streams, so uploads,
- * GEMMs and downloads of different blocks overlap and the link moves data in
- * both directions at once.  Device buffers (B plus three blocks of A and of
- * C) come from the library's per-device pool.  Ordered after the work
+ * locked memory lets the transfers run asynchronously and overlap).  A and B
+ * are uploaded in blocks of block_rows rows (0 = chosen: a quarter of the
+ * larger of M and N, rounded up to 256), alternately; the GEMM of each block
+ * of C starts as soon as its two blocks are up and the block comes back as
+ * soon as it is done, on three internal streams, so uploads, GEMMs and
+ * downloads overlap and the link moves data in both directions at once.
+ * Device buffers (A, B and four C blocks) come from the library's per-device
+ * pool.  Ordered after the work
  * already on `stream`, and `stream` waits for the result: the host buffers
  * must stay valid until then.  Strides as for b200_gemm_bf16 (no alignment
  * rule on the host side).  No reference counterpart (the reference takes

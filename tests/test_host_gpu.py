@@ -1,10 +1,12 @@
-"""b200_gemm_bf16_host / matmul_b200_host: operands in host memory, B uploaded
-once, A streamed in blocks of rows with uploads, GEMMs and downloads of
-different blocks overlapped on three streams.
+"""b200_gemm_bf16_host / matmul_b200_host: operands in host memory, A and B
+uploaded in alternating blocks of rows, the GEMM of each C block issued once
+its two blocks are up, uploads, GEMMs and downloads overlapped on three
+streams.
 
 Exact-arithmetic inputs must match the oracle bit for bit for every block
-size (ragged last blocks included); random inputs meet the parity bar and
-equal the device-resident GEMM wherever the blocks take the same kernel path.
+size (ragged last blocks included); random inputs meet the parity bar and,
+with whole-tile unsplit kernels forced on both sides, equal the
+device-resident GEMM bit for bit.
 """
 import numpy as np
 import pytest
@@ -47,21 +49,25 @@ def test_exact_inputs_bit_exact(M, N, K, block_rows):
 def test_random_matches_device_gemm(pinned):
     M, N, K = 3000, 2048, 2048
     A, Bt = workloads.make_operands(M, N, K, seed=5)
+    # whole-tile, unsplit kernels on both sides: every element then sums its
+    # K blocks in the same order, whatever the block shapes
     capi.set_stream_k(0)
+    capi.set_splits(1)
     try:
         C = host_gemm(A.cpu(), Bt.cpu(), 512, pinned)
     finally:
         capi.set_stream_k(1)
+        capi.set_splits(0)
     ref = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-    # whole-tile kernels on both sides (a stream-K tail sums split tiles in
-    # another grouping), so the bits must agree
     capi.set_stream_k(0)
+    capi.set_splits(1)
     try:
         assert capi.gemm_bf16(A.data_ptr(), Bt.data_ptr(), ref.data_ptr(), M, N, K, K, K, N,
                               0) == capi.OK
         torch.cuda.synchronize()
     finally:
         capi.set_stream_k(1)
+        capi.set_splits(0)
     assert torch.equal(C.view(torch.int16), ref.cpu().view(torch.int16))
     assert parity.passes(parity.metrics(C.cuda(), A.float() @ Bt.float().T, A, Bt))
 
