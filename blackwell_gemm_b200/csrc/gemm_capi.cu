@@ -893,8 +893,9 @@ int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int l
   // B200_GEMM_SKINNY=2 forces the cluster kernel for every M, 3 the
   // stream-K kernel.
   const int mode = skinny_mode();
-  if (epi == nullptr &&
-      (mode == 3 || (mode == 1 && !skinny_use_cluster(M, N, K) && M <= 64))) {
+  // (a forced slice count, b200_gemm_set_splits, takes the split-K kernels)
+  if (epi == nullptr && (mode == 3 || (mode == 1 && tuning_splits() == 0 &&
+                                       !skinny_use_cluster(M, N, K) && M <= 64))) {
     switch (skinny_slabs()) {
       case 1: return run_skinny_stream_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
       case 4: return run_skinny_stream_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
@@ -941,7 +942,8 @@ int skinny_slices(int M, int N, int K, const DeviceState* d) {
     return 1;
   }
   const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-  if (mode == 3 || (mode == 1 && !skinny_use_cluster(M, N, K) && M <= 64)) {
+  if (mode == 3 ||
+      (mode == 1 && forced == 0 && !skinny_use_cluster(M, N, K) && M <= 64)) {
     // stream-K: the most CTAs any one block of B is cut between
     const long long kb = ceil_div(K, skinny_fit_slabs(mp, skinny_slabs()) * kSlabK);
     const long long total = tiles * kb;
