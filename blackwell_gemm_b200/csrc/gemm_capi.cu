@@ -659,6 +659,15 @@ bool skinny_use_cluster(int M, int N, int K) {
   return M <= 8 || (M <= 16 && (long long)N * K < (32LL << 20));
 }
 
+// Per shape (mode 1), without a forced slice count: the stream-K kernel
+// from the cluster kernel's bound up to M = 128 (measured faster than the
+// persistent split-K kernel there at N, K = 4096..28672), the split-K kernel
+// above (its units of two blocks of B share A's slab; the stream-K kernel
+// re-reads A per block, twice B's bytes at M = 256).
+bool skinny_use_stream(int M, int N, int K) {
+  return tuning_splits() == 0 && !skinny_use_cluster(M, N, K) && M <= 128;
+}
+
 template <int kMp, int kSlabsWanted>
 int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
                   int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi) {
@@ -705,8 +714,8 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
 }
 
 // Stream-K skinny kernel (gemm_skinny_stream_kernel): G = min(SMs, work
-// items) CTAs, equal contiguous ranges of (tile, K block) items; partial
-// tiles meet in a per-call slot workspace whose flags are cleared first.
+// items) CTAs, equal contiguous ranges of (tile, K block) items, one
+// cooperative launch; partial tiles meet in a per-call slot workspace.
 long long stream_owner_host(long long x, long long total, int G) {
   return ((x + 1) * G + total - 1) / total - 1;
 }
@@ -767,9 +776,23 @@ int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, in
     if (cudaMemsetAsync(ws, 0, flag_bytes, stream) != cudaSuccess) st = B200_ERR_LAUNCH;
   }
   if (st == B200_OK) {
-    gemm_skinny_stream_kernel<kMp, kSlabs><<<G, P::kThreads, P::kSmemBytes, stream>>>(tb, ta, tc,
-                                                                                    args);
-    if (cudaGetLastError() != cudaSuccess) st = B200_ERR_LAUNCH;
+    // Cooperative: the fix-up waits on CTAs of higher index, so all G CTAs
+    // (one per SM) must be resident together.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)G, 1, 1);
+    cfg.blockDim = dim3(P::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = P::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, gemm_skinny_stream_kernel<kMp, kSlabs>, tb, ta, tc, args) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      st = B200_ERR_LAUNCH;
+    }
   }
   cudaFreeAsync(ws, stream);
   return st;
@@ -888,14 +911,13 @@ int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int l
                int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi = nullptr) {
   // Per shape (mode 1): for the fewest rows of A (skinny_use_cluster) the
   // single-launch cluster kernel (A's box is then mostly out of bounds, so
-  // nearly only B streams); up to 64 rows the stream-K kernel (all SMs, no
+  // nearly only B streams); up to 128 rows the stream-K kernel (all SMs, no
   // workspace clear or rounding pass); above, the persistent split-K kernel.
   // B200_GEMM_SKINNY=2 forces the cluster kernel for every M, 3 the
   // stream-K kernel.
   const int mode = skinny_mode();
   // (a forced slice count, b200_gemm_set_splits, takes the split-K kernels)
-  if (epi == nullptr && (mode == 3 || (mode == 1 && tuning_splits() == 0 &&
-                                       !skinny_use_cluster(M, N, K) && M <= 64))) {
+  if (epi == nullptr && (mode == 3 || (mode == 1 && skinny_use_stream(M, N, K)))) {
     switch (skinny_slabs()) {
       case 1: return run_skinny_stream_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
       case 4: return run_skinny_stream_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
@@ -942,8 +964,7 @@ int skinny_slices(int M, int N, int K, const DeviceState* d) {
     return 1;
   }
   const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-  if (mode == 3 ||
-      (mode == 1 && forced == 0 && !skinny_use_cluster(M, N, K) && M <= 64)) {
+  if (mode == 3 || (mode == 1 && skinny_use_stream(M, N, K))) {
     // stream-K: the most CTAs any one block of B is cut between
     const long long kb = ceil_div(K, skinny_fit_slabs(mp, skinny_slabs()) * kSlabK);
     const long long total = tiles * kb;

@@ -495,15 +495,24 @@ namespace b200 {
 // head of another:
 //   * a whole tile: the epilogue rounds TMEM to bf16 and TMA-stores C^T;
 //   * part of a tile: the epilogue writes the fp32 partial into slot j of
-//     the tile (j = this CTA's position among the tile's contributors, in K
-//     order) and raises flag (tile, j, lane quarter);
-//   * the CTA holding a tile's last K blocks (the tile is the first of its
-//     range) also finishes that tile after its range: it waits, bounded, for
-//     the earlier contributors' flags -- raised at the ends of their ranges --
-//     adds slots 0..j in K order, rounds and stores C.
-// Waits only point to CTAs of lower index, which the hardware dispatches
-// first.  Slots live in a per-call workspace; flags are raised to the call's
-// epoch (the launcher's per-stream flag arrays, or cleared per-call flags).
+//     the tile (j = this CTA's position among the tile's n contributors, in
+//     K order) and raises flag (tile, j, lane quarter).
+// After its range every contributor finishes a share of each partial tile
+// it touched: the tile's output is cut into pieces (lane quarter, 32
+// columns), contributor j takes pieces j, j + n, ... (for n = 2 the second
+// contributor takes all: it then waits only for the CTA below it, while a
+// share would make both wait for each other); for each it waits,
+// bounded, for the n flags of the piece's quarter, loads the n slot
+// granules of the piece, adds them in K order, rounds and stores C.
+// Spreading the fix-up this way keeps
+// every SM's share of slot reads at about one slot per partial tile; a
+// single finishing CTA per tile read all n slots and was the critical path.
+// A slot is laid out [lane quarter][Mp m][32 n] fp32, so a piece of a slot
+// (kChunk x 32 floats) is contiguous.
+// Contributors wait for CTAs of higher index too, so the launch is
+// cooperative: all G CTAs are resident together.  Slots live in a per-call
+// workspace; flags are raised to the call's epoch (the launcher's per-stream
+// flag arrays, or cleared per-call flags).
 struct SkinnyStreamArgs {
   int M, N, K;
   int l2_hint;
@@ -511,7 +520,7 @@ struct SkinnyStreamArgs {
   int k_blocks;      // K blocks per tile, ceil(K / kBK)
   long long total;   // tiles x k_blocks
   int max_seg;       // slots per tile
-  float* slots;      // [tiles][max_seg][kMp][128] fp32
+  float* slots;      // [tiles][max_seg][4 quarters][kMp][32] fp32
   unsigned int* flags;  // [tiles][max_seg][4], below `epoch` at launch
   unsigned int epoch;   // value a raised flag takes in this call
   int* status;
@@ -665,15 +674,18 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
     // Epilogue: warp w holds TMEM lanes 32 (w % 4) .. + 31 = rows n of B
     // (columns of C); register j of a chunk is row m = c kChunk + j of C.
     const int quarter = warp & 3;
-    const int n_local = quarter * 32 + lane;
     const uint32_t my_store = store_base + (warp - 2) * 2 * P::kStoreBuf;
     uint32_t nstore = 0;
     int it = 0;
-    int fix_tile = -1, fix_slots = 0;  // tile this CTA finishes after its range
+    // Partial tiles of this range (at most two: the first and the last
+    // segment), finished after the range: tile, this CTA's slot, slots.
+    int fix_t[2] = {0, 0}, fix_j[2] = {0, 0}, fix_n[2] = {0, 0};
+    int nfix = 0;
     bool alive = true;
     // Rounds 32 (or Mp) rows of C held as fp32 bits in v and TMA-stores them
-    // through this warp's staging buffers ([kChunk m][32 n] bf16).
-    auto store_bf16 = [&](const uint32_t* v, int t, int c) {
+    // through this warp's staging buffers ([kChunk m][32 n] bf16) at lane
+    // quarter q of tile t.
+    auto store_bf16 = [&](const uint32_t* v, int t, int q, int c) {
       const uint32_t sb = my_store + (nstore & 1u) * P::kStoreBuf;
       if (lane == 0) bulk_wait_group_read<1>();
       __syncwarp();
@@ -685,7 +697,7 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_store_2d(&tmap_c, sb, t * P::kRowsB + quarter * 32, c * kChunk);
+        tma_store_2d(&tmap_c, sb, t * P::kRowsB + q * 32, c * kChunk);
         bulk_commit_group();
       }
       ++nstore;
@@ -702,8 +714,10 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
       tc_fence_after_sync();
       const uint32_t tbase = tmem_base + buf * kMp + ((uint32_t)(quarter * 32) << 16);
       const bool whole = kb0 == 0 && kb1 == KB;
-      const int j = (int)blockIdx.x - stream_owner((long long)t * KB, args.total, G);
-      float* slot = args.slots + (((long long)t * args.max_seg + j) * kMp) * P::kRowsB + n_local;
+      const int first = stream_owner((long long)t * KB, args.total, G);
+      const int j = (int)blockIdx.x - first;
+      float* slot = args.slots + ((long long)t * args.max_seg + j) * kMp * P::kRowsB +
+                    quarter * kMp * 32 + lane;
 #pragma unroll 1
       for (int c = 0; c < kMp / kChunk; ++c) {
         uint32_t v[kChunk];
@@ -718,38 +732,86 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
           if (lane == 0) mbar_arrive_local(smem_u32(&bar_acc_empty[buf]));
         }
         if (whole) {
-          store_bf16(v, t, c);
+          store_bf16(v, t, quarter, c);
         } else {
-          // slot[m][n_local]: each warp-wide store covers 128 contiguous bytes
+          // slot[quarter][m][lane]: each warp-wide store covers 128 contiguous bytes
 #pragma unroll
-          for (int jj = 0; jj < kChunk; ++jj)
-            slot[(long long)(c * kChunk + jj) * P::kRowsB] = __uint_as_float(v[jj]);
+          for (int jj = 0; jj < kChunk; ++jj) slot[(c * kChunk + jj) * 32] = __uint_as_float(v[jj]);
         }
       }
       if (!whole) {
-        if (kb1 == KB) {
-          fix_tile = t;  // this CTA holds the tile's last K blocks: it finishes it
-          fix_slots = j + 1;
-        } else {
+        const int n = stream_owner((long long)t * KB + KB - 1, args.total, G) - first + 1;
+        // (With two contributors the second finishes the tile from its own
+        // quarters of its own slot: no other warp reads them.)
+        if (n != 2 || j != 1) {
           asm volatile("fence.acq_rel.gpu;" ::: "memory");
           __syncwarp();
           if (lane == 0)
             st_release_gpu_u32(args.flags + ((long long)t * args.max_seg + j) * 4 + quarter,
                                args.epoch);
         }
+        if (nfix < 2) {
+          fix_t[nfix] = t;
+          fix_j[nfix] = j;
+          fix_n[nfix] = n;
+          ++nfix;
+        }
       }
       ++it;
     })
-    if (alive && fix_tile >= 0) {
-      // Finish the tile: wait for the earlier contributors' slots, add all
-      // slots in K order, round, store.
-      const long long tslots = (long long)fix_tile * args.max_seg;
-      bool ready = true;
-      for (int s = 0; ready && s < fix_slots - 1; ++s) {
-        const unsigned int* f = args.flags + (tslots + s) * 4 + quarter;
+    // Finish the partial tiles.  A tile's output is cut into pieces (lane
+    // quarter q, chunk c); contributor j of the tile's n finishes pieces
+    // j, j + n, j + 2n, ..., dealt in turn over its four epilogue warps
+    // (n = 2: contributor 1 finishes all of them, each warp its quarter).  A
+    // warp waits, bounded, for all flags of its tiles (one warp-wide poll
+    // covers a tile's 4n flags), then loads the pieces' slot granules with
+    // 16-byte loads, adds each piece's n granules in K order, rounds and
+    // stores it.  (Bulk copies of the granules
+    // need a generic-to-async proxy fence first, which waits for this
+    // warp's C stores still in flight and cost more than the loads.)
+    constexpr int kChunks = kMp / kChunk;
+    constexpr int kPieces = 4 * kChunks;
+    // At most a whole tile (n = 2) plus a third of another (n >= 3).
+    constexpr int kMaxMine = (kPieces + kPieces / 3) / 4 + 2;
+    int mine[kMaxMine];  // (f << 8) | piece
+    int nmine = 0;
+    int has = 0;  // bit f: this warp finishes pieces of tile f
+    {
+      int dealt = 0;
+#pragma unroll 1
+      for (int f = 0; f < nfix; ++f) {
+        if (fix_n[f] == 2) {
+          // Two contributors: the second (whose range starts with the tile,
+          // so its partial is ready first) finishes the whole tile, each
+          // warp its own lane quarter, and waits only for the CTA below it.
+          if (fix_j[f] == 1)
+#pragma unroll 1
+            for (int pc = quarter; pc < kPieces && nmine < kMaxMine; pc += 4) {
+              mine[nmine++] = (f << 8) | pc;
+              has |= 1 << f;
+            }
+          continue;
+        }
+#pragma unroll 1
+        for (int pc = fix_j[f]; pc < kPieces; pc += fix_n[f], ++dealt)
+          if ((dealt & 3) == warp - 2 && nmine < kMaxMine) {
+            mine[nmine++] = (f << 8) | pc;
+            has |= 1 << f;
+          }
+      }
+    }
+#pragma unroll 1
+    for (int f = 0; alive && f < nfix; ++f) {
+      if (!((has >> f) & 1)) continue;
+      const unsigned int* tflags = args.flags + (long long)fix_t[f] * args.max_seg * 4;
+      // flags of slots other than this CTA's own when it finishes alone
+      const int nflags = fix_n[f] == 2 ? 4 : 4 * fix_n[f];
+#pragma unroll 1
+      for (int base = 0; alive && base < nflags; base += 32) {
+        const int idx = base + lane;
         const unsigned long long t0 = globaltimer_ns();
         for (;;) {
-          const bool up = (int)(ld_acquire_gpu_u32(f) - args.epoch) >= 0;
+          const bool up = idx >= nflags || (int)(ld_acquire_gpu_u32(tflags + idx) - args.epoch) >= 0;
           if (__all_sync(0xffffffffu, up)) break;
           int give_up = 0;
           if (lane == 0 && globaltimer_ns() - t0 > args.timeout_ns) {
@@ -757,29 +819,86 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
             give_up = 1;
           }
           if (__shfl_sync(0xffffffffu, give_up, 0)) {
-            ready = false;
+            alive = false;
             break;
           }
-          __nanosleep(128);
+          __nanosleep(64);
         }
       }
-      if (ready) {
-        const float* base = args.slots + tslots * kMp * P::kRowsB + n_local;
-#pragma unroll 1
-        for (int c = 0; c < kMp / kChunk; ++c) {
-          float acc[kChunk];
+    }
+    __syncwarp();  // orders every lane after the flags the other lanes acquired
+    // A granule (kChunk m x 32 n fp32) is kVec float4 per lane: float4 i of
+    // lane l holds m = l / 8 + 4 i, n = 4 (l % 8) .. + 3.  The granules of
+    // this warp's pieces are loaded in sequence (piece by piece, slots in K
+    // order), kRound at a time whatever piece they belong to; a piece is
+    // rounded and stored when its last granule has been added.
+    constexpr int kVec = kChunk / 4;
+    constexpr int kRound = 4;
+    const long long slot_floats = (long long)kMp * P::kRowsB;
+    auto granule = [&](int x, int sl) {
+      const int f = mine[x] >> 8, pc = mine[x] & 255;
+      return args.slots + ((long long)fix_t[f] * args.max_seg + sl) * slot_floats +
+             ((pc & 3) * kMp + (pc >> 2) * kChunk) * 32 + 4 * lane;
+    };
+    auto store_piece = [&](const float4* acc, int x) {
+      const int f = mine[x] >> 8, pc = mine[x] & 255;
+      const uint32_t sb = my_store + (nstore & 1u) * P::kStoreBuf;
+      if (lane == 0) bulk_wait_group_read<1>();
+      __syncwarp();
 #pragma unroll
-          for (int jj = 0; jj < kChunk; ++jj) acc[jj] = 0.f;
-#pragma unroll 1
-          for (int s = 0; s < fix_slots; ++s) {
-            const float* p = base + ((long long)s * kMp + c * kChunk) * P::kRowsB;
+      for (int i = 0; i < kVec; ++i) {
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(acc[i].x, acc[i].y);
+        const __nv_bfloat162 hi = __floats2bfloat162_rn(acc[i].z, acc[i].w);
+        st_shared_v2(sb + (((lane >> 3) + 4 * i) * 32 + 4 * (lane & 7)) * 2u,
+                     *reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&tmap_c, sb, fix_t[f] * P::kRowsB + (pc & 3) * 32, (pc >> 2) * kChunk);
+        bulk_commit_group();
+      }
+      ++nstore;
+    };
+    float4 acc[kVec];
 #pragma unroll
-            for (int jj = 0; jj < kChunk; ++jj) acc[jj] += __ldcg(p + (long long)jj * P::kRowsB);
+    for (int i = 0; i < kVec; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    int lx = 0, ls = 0;  // next granule to load: piece lx, slot ls
+#pragma unroll 1
+    while (alive && lx < nmine) {
+      float4 xv[kRound][kVec];
+      int gx[kRound];
+      int cnt = 0;
+#pragma unroll
+      for (int u = 0; u < kRound; ++u) {
+        if (lx < nmine) {
+          const float* g = granule(lx, ls);
+#pragma unroll
+          for (int i = 0; i < kVec; ++i) xv[u][i] = ld_global_cg_v4(g + 128 * i);
+          gx[u] = lx;
+          if (++ls == fix_n[mine[lx] >> 8]) {
+            ls = 0;
+            ++lx;
           }
-          uint32_t v[kChunk];
+          cnt = u + 1;
+        }
+      }
 #pragma unroll
-          for (int jj = 0; jj < kChunk; ++jj) v[jj] = __float_as_uint(acc[jj]);
-          store_bf16(v, fix_tile, c);
+      for (int u = 0; u < kRound; ++u) {
+        if (u < cnt) {
+#pragma unroll
+          for (int i = 0; i < kVec; ++i) {
+            acc[i].x += xv[u][i].x;
+            acc[i].y += xv[u][i].y;
+            acc[i].z += xv[u][i].z;
+            acc[i].w += xv[u][i].w;
+          }
+          const bool last = u + 1 < cnt ? gx[u + 1] != gx[u] : lx > gx[u];
+          if (last) {
+            store_piece(acc, gx[u]);
+#pragma unroll
+            for (int i = 0; i < kVec; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
         }
       }
     }

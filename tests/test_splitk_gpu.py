@@ -218,10 +218,28 @@ def test_skinny_kernel_forced_splits_random(splits):
     assert parity.passes(parity.metrics(C, A.float() @ Bt.float().T, A, Bt))
 
 
-def test_skinny_stream_k_graph_replays_and_streams():
-    """The stream-K skinny kernel (16 < M <= 64 by default) raises per-stream
+@pytest.mark.parametrize("M,N,K", [(128, 24576, 1024), (128, 12288, 1024), (100, 4096, 2048),
+                                   (256, 8192, 1024), (64, 1024, 8192)])
+def test_skinny_stream_k_fixup_exact_bits(M, N, K):
+    """The stream-K skinny kernel over its fix-up structures: blocks of B
+    split between two CTAs (the second finishes the block alone), between
+    three to six (every contributor finishes a share), mixtures of both, and
+    about twenty contributors to a block (more than its pieces, so some
+    contributors finish nothing)."""
+    capi.set_skinny_mode(3)
+    try:
+        A, Bt = oracle.exact_inputs(M, N, K, seed=M + N)
+        C = bf16_gemm(dev(A), dev(Bt))
+        assert np.array_equal(bits(C), oracle.gemm_bf16(A, Bt))
+    finally:
+        capi.set_skinny_mode(1)
+
+
+@pytest.mark.parametrize("M", [48, 128])
+def test_skinny_stream_k_graph_replays_and_streams(M):
+    """The stream-K skinny kernel (16 < M <= 128 by default) raises per-stream
     epoch flags outside capture and clears its own flags when captured."""
-    M, N, K = 48, 4096, 8192
+    N, K = 4096, 8192
     A, Bt = workloads.make_operands(M, N, K, seed=31, weight_std=0.02)
     ref = bf16_gemm(A, Bt).clone()
     C = torch.zeros(M, N, dtype=torch.bfloat16, device="cuda")
@@ -231,6 +249,7 @@ def test_skinny_stream_k_graph_replays_and_streams():
                               stream) == capi.OK
 
     side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())  # C's zero fill
     call(C, side.cuda_stream)
     torch.cuda.synchronize()
     assert torch.equal(C.view(torch.int16), ref.view(torch.int16))
@@ -244,6 +263,8 @@ def test_skinny_stream_k_graph_replays_and_streams():
         assert torch.equal(C.view(torch.int16), ref.view(torch.int16))
     outs = [torch.zeros_like(C) for _ in range(2)]
     streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for st in streams:
+        st.wait_stream(torch.cuda.current_stream())
     for _ in range(3):
         for s, out in zip(streams, outs):
             call(out, s.cuda_stream)
