@@ -333,6 +333,10 @@ def main():
                          "ksplit: 8192 x 8192 x 131072 with K split across the GPUs, "
                          "reduced inside the GEMM kernel over NVLink; "
                          "sweep: every single-GPU configuration shape, one line each")
+    ap.add_argument("--shapes", default="",
+                    help="with --mode sweep: comma-separated MxNxK shapes to time instead "
+                         "of the configuration shapes (weights N(0, 0.02) for M <= 256, "
+                         "the skinny rule, else N(0, 1))")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -610,9 +614,15 @@ def run_sweep(args, world, rank, dev):
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
     steps = max(10, min(args.steps, 50))
-    for name in ("square_1024", "square", "projection", "skinny"):
-        for (M, N, K) in CONFIGS[name]:
-            A, Bt = make_operands(M, N, K, seed=M + N + K, weight_std=WEIGHT_STD[name], device=dev)
+    if args.shapes:
+        custom = [tuple(int(v) for v in sh.lower().split("x")) for sh in args.shapes.split(",")]
+        groups = [("skinny" if M <= 256 else "shape", [(M, N, K)]) for M, N, K in custom]
+    else:
+        groups = [(name, CONFIGS[name]) for name in ("square_1024", "square", "projection", "skinny")]
+    for name, shapes in groups:
+        for (M, N, K) in shapes:
+            std = WEIGHT_STD.get(name, WEIGHT_STD["skinny"] if M <= 256 else WEIGHT_STD["square"])
+            A, Bt = make_operands(M, N, K, seed=M + N + K, weight_std=std, device=dev)
             C = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
             gemm_ours(A, Bt, C, stream)
             torch.cuda.synchronize()
