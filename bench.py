@@ -259,7 +259,7 @@ def e2e_measure(gemm, A, Bt, stream, steps=8, warmup=2):
 
 def e2e_measure_host(A, Bt, stream, steps=8, warmup=2):
     """Our public host-memory entry point, b200_gemm_bf16_host: pinned host A,
-    B and C; inside each call B is uploaded, A streams in blocks whose
+    B and C; inside each call A and B go up in alternating blocks whose
     uploads, GEMMs and C downloads overlap.  CUDA events on the caller's
     stream bracket the calls (the call orders itself after, and releases,
     that stream)."""
@@ -289,6 +289,39 @@ def e2e_measure_host(A, Bt, stream, steps=8, warmup=2):
     # the result that came back, checked like the device result
     par = parity_sample(hC.to(A.device), A, Bt)
     return ms, 2 * (M * K + N * K), 2 * M * N, par
+
+
+def link_floor_ms(h2d_bytes, d2h_bytes, dev, reps=3):
+    """The PCIe floor of one e2e step: its host->device and device->host bytes
+    copied at the same time on two streams, pinned host memory, CUDA events on
+    the caller's stream around both (best of `reps` after one warm-up).  The
+    link is not full duplex at full rate, so this is below max(up, down)
+    at the one-way rates."""
+    hu = torch.empty(h2d_bytes, dtype=torch.uint8).pin_memory()
+    hd = torch.empty(d2h_bytes, dtype=torch.uint8).pin_memory()
+    du = torch.empty(h2d_bytes, dtype=torch.uint8, device=dev)
+    dd = torch.empty(d2h_bytes, dtype=torch.uint8, device=dev)
+    main = torch.cuda.current_stream(dev)
+    s_up, s_down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    best = None
+    for r in range(reps + 1):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(main)
+        s_up.wait_stream(main)
+        s_down.wait_stream(main)
+        with torch.cuda.stream(s_up):
+            du.copy_(hu, non_blocking=True)
+        with torch.cuda.stream(s_down):
+            hd.copy_(dd, non_blocking=True)
+        main.wait_stream(s_up)
+        main.wait_stream(s_down)
+        e1.record(main)
+        torch.cuda.synchronize(dev)
+        if r:
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+    return best
 
 
 def cpu_baseline(Bt, rows=256):
@@ -413,14 +446,22 @@ def main():
     if not args.no_extras:
         e_ms, h2d, d2h, same = e2e_measure_host(A, Bt, stream)
         s_ms, _, _ = e2e_measure(gemm_ours, A, Bt, stream)
-        et = torch.tensor([e_ms, s_ms], dtype=torch.float64, device=dev)
+        f_ms = link_floor_ms(h2d, d2h, dev)
+        et = torch.tensor([e_ms, s_ms, f_ms], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(et, op=dist.ReduceOp.MAX)
         e2e = {"value": flops_step * world / (float(et[0]) * 1e-3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
                "ms_per_step": float(et[0]),
                "path": "capi.gemm_bf16_host (b200_gemm_bf16_host) with pinned host A, B and C: "
-                       "B uploaded, A streamed in blocks, uploads / GEMMs / downloads overlapped",
+                       "A and B uploaded in alternating blocks, each block of C computed once "
+                       "its two blocks are up and downloaded once done, uploads / GEMMs / "
+                       "downloads overlapped on three streams",
+               "link_floor": {"ms_per_step": float(et[2]),
+                              "value": flops_step * world / (float(et[2]) * 1e-3) / 1e12,
+                              "frac": float(et[2]) / float(et[0]),
+                              "what": "the step's upload and download bytes copied at once on "
+                                      "two streams (pinned memory), no GEMM: the PCIe floor"},
                "parity": same,
                "serial_copies": {"value": flops_step * world / (float(et[1]) * 1e-3) / 1e12,
                                  "ms_per_step": float(et[1]),
