@@ -99,7 +99,7 @@ def test_argument_checks():
         capi.ksplit_destroy(comm)
 
 
-# ------------------------------------------------------------ two GPUs
+# -------------------------------------------------------- several GPUs
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -123,6 +123,8 @@ def _worker(rank, world, port, q):
         # random operands, several calls (256- then 512-wide pair tiles): bits
         # equal to the NCCL path, parity against fp32
         calls = [(2048, 1536, 4096), (2048, 1536, 4096), (1024, 1000, 2048), (2048, 1536, 1024)]
+        # (each rank owns whole 256-row pair-tile rows of C)
+        calls = [c for c in calls if c[0] % (world * 256) == 0]
         for call, (M, N, K) in enumerate(calls + calls):
             capi.set_tuning(256 if call < len(calls) else 512, 1, 0)
             A, Bt = workloads.make_operands(M, N, K, seed=100 + call, device=dev)
@@ -172,13 +174,15 @@ def _worker(rank, world, port, q):
         q.put((rank, False, traceback.format_exc()))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_fused_k_split_on_two_gpus():
+@pytest.mark.parametrize("world", [2, 4])
+def test_fused_k_split_on_several_gpus(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in ps:
         p.start()
     res = [q.get(timeout=300) for _ in ps]
