@@ -156,10 +156,10 @@ def _worker(rank, world, port, q):
 
         # A peer that never joins a call: rank 0 calls alone, its own-tile waits
         # run out (5 x 0.2 s) and the kernel returns with the error word set.
-        fk = bdist.FusedKSplit(512, 256)
+        fk = bdist.FusedKSplit(256 * world, 256)  # one pair-tile row per rank
         capi.set_wait_timeout_ns(200_000_000)
         if rank == 0:
-            A, Bt = workloads.make_operands(512, 256, 128, seed=1, device=dev)
+            A, Bt = workloads.make_operands(256 * world, 256, 128, seed=1, device=dev)
             fk(A, Bt)
             torch.cuda.synchronize()
             st = capi.device_status(True)
