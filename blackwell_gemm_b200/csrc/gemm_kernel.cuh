@@ -35,6 +35,12 @@
 #include "ksplit_fused.cuh"
 #include "sm100_ptx.cuh"
 
+// TMEM loads (32 columns each) in flight per wait when a 512-wide tile's
+// epilogue drains its single accumulator into registers (plain bf16 output).
+#ifndef B200_DRAIN_BATCH
+#define B200_DRAIN_BATCH 4
+#endif
+
 namespace b200 {
 
 struct EpiArgs {
@@ -845,16 +851,28 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
         }
         // Drain this warp's 32 x 256 slice into registers as packed bf16
         // (128 registers per thread), release the accumulator, then store.
+        // The MMA of the next tile waits for this drain (single accumulator),
+        // so the loads go out kDrainBatch at a time with one wait each: the
+        // drain takes kSubN / 32 / kDrainBatch load latencies, not kSubN / 32.
+        // (One at a time where the K-split sums or the profiler need the
+        // registers: batching there spills.)
+        constexpr int kDrainBatch = (kOut == kOutBf16 && !kProfile) ? B200_DRAIN_BATCH : 1;
+        static_assert((kSubN / 32) % kDrainBatch == 0, "drain batch must divide the chunks");
         uint32_t packed[kSubN / 2];
 #pragma unroll
-        for (int c = 0; c < kSubN / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, v);
-          tmem_wait_ld();
-          if constexpr (kOut == kOutKsplit)
-            ks_accumulate(v, recv, recv_stride, c, args.ks.rank, args.ks.nranks);
+        for (int c = 0; c < kSubN / 32; c += kDrainBatch) {
+          uint32_t v[kDrainBatch][32];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) packed[c * 16 + i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+          for (int b = 0; b < kDrainBatch; ++b) tmem_ld_32x32b_x32(tbase + (c + b) * 32, v[b]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int b = 0; b < kDrainBatch; ++b) {
+            if constexpr (kOut == kOutKsplit)
+              ks_accumulate(v[b], recv, recv_stride, c + b, args.ks.rank, args.ks.nranks);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              packed[(c + b) * 16 + i] = pack_bf16x2(v[b][2 * i], v[b][2 * i + 1]);
+          }
         }
         tc_fence_before_sync();
         __syncwarp();
