@@ -32,7 +32,7 @@ extern "C" {
 #define B200_ERR_UNSUPPORTED_DEVICE 3 /* current device is not sm_100 */
 #define B200_ERR_TENSOR_MAP 4       /* cuTensorMapEncodeTiled rejected the operand */
 #define B200_ERR_LAUNCH 5           /* CUDA error at or before the launch */
-#define B200_ERR_DEVICE_TIMEOUT 6   /* a kernel pipeline wait ran out (see device_status) */
+#define B200_ERR_DEVICE_TIMEOUT 6   /* reserved: timeouts are read with b200_gemm_device_status */
 #define B200_ERR_TOO_LARGE 7        /* a size exceeds what the entry point supports */
 
 /* C = A * B^T, bf16 in and out, fp32 accumulation.
