@@ -61,6 +61,12 @@ SIGNATURES = {
     "b200_gemm_status_string": (ctypes.c_char_p, [_i]),
     "b200_gemm_tile_coord": (None, [_i, _i, _i, _i, _ip, _ip]),
     "b200_gemm_idesc": (_u32, [_i, _i]),
+    "b200_gemm_sk_range_pairs": (_i, [ctypes.c_longlong, _i]),
+    "b200_gemm_sk_range": (None, [_i, ctypes.c_longlong, _i, ctypes.POINTER(ctypes.c_longlong),
+                                  ctypes.POINTER(ctypes.c_longlong)]),
+    "b200_gemm_sk_owner": (_i, [ctypes.c_longlong, ctypes.c_longlong, _i]),
+    "b200_gemm_sk_next_segment": (None, [ctypes.c_longlong, ctypes.POINTER(ctypes.c_longlong), _i,
+                                         _ip, _ip, _ip]),
     "b200_gemm_smem_desc": (_u64, [_u32]),
     "b200_gemm_launch_shape": (_i, [_i, _i, _i, _ip, _ip, _ip, _ip]),
     "b200_ksplit_create": (_i, [_i, _i, _i, _i, ctypes.POINTER(_vp), _vp]),
@@ -210,6 +216,32 @@ def tile_coord(t: int, tiles_m: int, tiles_n: int, group: int):
 
 def idesc(mma_m: int, mma_n: int) -> int:
     return lib().b200_gemm_idesc(mma_m, mma_n)
+
+
+def sk_range_pairs(items: int, pairs: int) -> int:
+    return lib().b200_gemm_sk_range_pairs(items, pairs)
+
+
+def sk_range(pair: int, items: int, range_pairs: int):
+    lo, hi = ctypes.c_longlong(0), ctypes.c_longlong(0)
+    lib().b200_gemm_sk_range(pair, items, range_pairs, ctypes.byref(lo), ctypes.byref(hi))
+    return lo.value, hi.value
+
+
+def sk_owner(x: int, items: int, range_pairs: int) -> int:
+    return lib().b200_gemm_sk_owner(x, items, range_pairs)
+
+
+def sk_segments(lo: int, hi: int, k_blocks: int):
+    """A pair's stream-K segments in the kernel's order: [(tile, kb0, kb1), ...]."""
+    pos = ctypes.c_longlong(hi)
+    t, kb0, kb1 = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    out = []
+    while pos.value > lo:
+        lib().b200_gemm_sk_next_segment(lo, ctypes.byref(pos), k_blocks, ctypes.byref(t),
+                                        ctypes.byref(kb0), ctypes.byref(kb1))
+        out.append((t.value, kb0.value, kb1.value))
+    return out
 
 
 def smem_desc(addr: int) -> int:

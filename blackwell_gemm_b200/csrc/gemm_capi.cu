@@ -1538,6 +1538,22 @@ void b200_gemm_tile_coord(int t, int tiles_m, int tiles_n, int group, int* tm, i
 
 uint32_t b200_gemm_idesc(int mma_m, int mma_n) { return make_idesc_bf16_f32(mma_m, mma_n); }
 
+int b200_gemm_sk_range_pairs(long long items, int pairs) { return sk_range_pairs(items, pairs); }
+
+void b200_gemm_sk_range(int pair, long long items, int range_pairs, long long* lo,
+                        long long* hi) {
+  sk_range(pair, items, range_pairs, lo, hi);
+}
+
+int b200_gemm_sk_owner(long long x, long long items, int range_pairs) {
+  return sk_owner(x, items, range_pairs);
+}
+
+void b200_gemm_sk_next_segment(long long lo, long long* pos, int k_blocks, int* t, int* kb0,
+                               int* kb1) {
+  sk_next_segment(lo, pos, k_blocks, t, kb0, kb1);
+}
+
 uint64_t b200_gemm_smem_desc(uint32_t smem_addr) { return make_sdesc_k128(smem_addr); }
 
 int b200_ksplit_create(int rank, int nranks, int max_m, int max_n, b200_ksplit_comm** comm,

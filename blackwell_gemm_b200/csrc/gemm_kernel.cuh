@@ -390,16 +390,10 @@ __device__ __forceinline__ void unit_coord(int u, const GemmArgs& a, int* tm, in
   *kb1 = end < a.k_blocks ? end : a.k_blocks;
 }
 
-// First pair (of G) whose stream-K range [p items / G, (p+1) items / G)
-// holds item x.
-__device__ __forceinline__ int sk_owner(long long x, long long items, int G) {
-  return (int)(((x + 1) * G + items - 1) / items) - 1;
-}
-
 // Pairs taking stream-K work: all P, or one per item when there are fewer
-// items, so that no range is empty.
+// items, so that no range is empty (sk_range_pairs, gemm_layout.h).
 __device__ __forceinline__ int sk_pairs(const GemmArgs& a, int P) {
-  return a.sk_items < P ? (int)a.sk_items : P;
+  return sk_range_pairs(a.sk_items, P);
 }
 
 // One pair's work, in order: its stream-K segments (a tile and a K-block
@@ -417,10 +411,7 @@ struct WorkIter {
     dp_units = a.dp_tiles * a.splits;
     lo = pos = 0;
     const int G = sk_pairs(a, P);
-    if (a.sk_tiles > 0 && pair < G) {
-      lo = (long long)pair * a.sk_items / G;
-      pos = (long long)(pair + 1) * a.sk_items / G;
-    }
+    if (a.sk_tiles > 0 && pair < G) sk_range(pair, a.sk_items, G, &lo, &pos);
   }
   // Next work: tile (tm, tn), K blocks [kb0, kb1), stream-K tile index sk_t
   // (-1 for a data-parallel unit).  False when the pair's work is done.
@@ -429,14 +420,10 @@ struct WorkIter {
                                        int* sk_t) {
     if constexpr (kSK) {
       if (pos > lo) {
-        const int KB = a.k_blocks;
-        const int t = (int)((pos - 1) / KB);
-        const long long base = (long long)t * KB;
-        *kb1 = (int)(pos - base);
-        *kb0 = lo > base ? (int)(lo - base) : 0;
+        int t;
+        sk_next_segment(lo, &pos, a.k_blocks, &t, kb0, kb1);
         tile_coord(a.dp_tiles + t, a.tiles_m, a.tiles_n, a.group, tm, tn);
         *sk_t = t;
-        pos = base + *kb0;
         return true;
       }
     }

@@ -142,4 +142,39 @@ B200_HD void tile_coord(int t, int tiles_m, int tiles_n, int group, int* tm, int
   *tn = cols ? a : b;
 }
 
+// ---------------------------------------------------------------------------
+// Stream-K split of the tail tiles (shared by the kernel and the CPU tests).
+// The tail's (tile, K block) items, item = tile * k_blocks + kb, are cut into
+// G contiguous ranges, pair p taking [p items / G, (p+1) items / G), where G
+// = min(pairs, items) so that no range is empty.
+
+B200_HD int sk_range_pairs(long long items, int pairs) {
+  return items < pairs ? (int)items : pairs;
+}
+
+B200_HD void sk_range(int pair, long long items, int G, long long* lo, long long* hi) {
+  *lo = (long long)pair * items / G;
+  *hi = (long long)(pair + 1) * items / G;
+}
+
+// First pair (of G) whose range holds item x.
+B200_HD int sk_owner(long long x, long long items, int G) {
+  return (int)(((x + 1) * G + items - 1) / items) - 1;
+}
+
+// Next segment of a pair's range [lo, *pos), walked from its end: the tile
+// holding item *pos - 1 and its K blocks [kb0, kb1) inside the range; moves
+// *pos to the segment's first item.  A pair thus meets first the head of the
+// tile it shares with the next pair and last the tail of the tile it
+// finishes.  Requires *pos > lo.
+B200_HD void sk_next_segment(long long lo, long long* pos, int k_blocks, int* t, int* kb0,
+                             int* kb1) {
+  const int tile = (int)((*pos - 1) / k_blocks);
+  const long long base = (long long)tile * k_blocks;
+  *kb1 = (int)(*pos - base);
+  *kb0 = lo > base ? (int)(lo - base) : 0;
+  *t = tile;
+  *pos = base + *kb0;
+}
+
 }  // namespace b200

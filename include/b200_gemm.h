@@ -229,6 +229,17 @@ int b200_ksplit_destroy(b200_ksplit_comm* comm);
 /* Host-side layout rules, exported so they can be checked without a GPU. */
 void b200_gemm_tile_coord(int t, int tiles_m, int tiles_n, int group, int* tm, int* tn);
 uint32_t b200_gemm_idesc(int mma_m, int mma_n);
+/* Stream-K split of a tail of `items` (tile, K block) items over `pairs`
+ * pairs, as the kernel computes it: pairs taking work (min(pairs, items)),
+ * pair p's item range [*lo, *hi), the first pair whose range holds item x,
+ * and the next segment (tile, K blocks [kb0, kb1)) of a range walked from
+ * its end (*pos moves to the segment's first item).  No reference
+ * counterpart (the reference deals whole tiles). */
+int b200_gemm_sk_range_pairs(long long items, int pairs);
+void b200_gemm_sk_range(int pair, long long items, int range_pairs, long long* lo, long long* hi);
+int b200_gemm_sk_owner(long long x, long long items, int range_pairs);
+void b200_gemm_sk_next_segment(long long lo, long long* pos, int k_blocks, int* t, int* kb0,
+                               int* kb1);
 uint64_t b200_gemm_smem_desc(uint32_t smem_addr);
 /* Launch geometry the GEMM would use: pair tiles, grid CTAs (0 if no
  * device), dynamic shared memory bytes and threads per CTA. */

@@ -133,3 +133,64 @@ def test_launch_shape_without_gpu():
             assert s["smem_bytes"] <= 227 * 1024
     finally:
         capi.set_tuning(before["tile_n"] or -1, before["stage_slabs"], before["raster_group"])
+
+
+def _check_stream_k_split(sk_tiles, k_blocks, pairs):
+    items = sk_tiles * k_blocks
+    G = capi.sk_range_pairs(items, pairs)
+    assert G == min(items, pairs)
+    covered = {}
+    nonfinishing = {}          # pair -> tile of its one unfinished piece
+    finisher = {}              # tile -> pair holding its last K block
+    prev_hi = 0
+    for p in range(G):
+        lo, hi = capi.sk_range(p, items, G)
+        assert lo == prev_hi and hi > lo      # contiguous, non-empty
+        prev_hi = hi
+        segs = capi.sk_segments(lo, hi, k_blocks)
+        pos = hi
+        for i, (t, kb0, kb1) in enumerate(segs):
+            # walked from the end, one tile per segment, exactly covering the range
+            assert 0 <= kb0 < kb1 <= k_blocks
+            assert t * k_blocks + kb1 == pos
+            pos = t * k_blocks + kb0
+            for kb in range(kb0, kb1):
+                assert (t, kb) not in covered
+                covered[(t, kb)] = p
+            if kb1 < k_blocks:
+                # a piece left for another pair: at most one per pair (one slot),
+                # and it is the pair's first segment
+                assert p not in nonfinishing and i == 0
+                nonfinishing[p] = t
+            else:
+                finisher[t] = p
+        assert pos == lo
+    assert prev_hi == items and len(covered) == items
+    for t in range(sk_tiles):
+        f = finisher[t]
+        c0 = capi.sk_owner(t * k_blocks, items, G)
+        assert covered[(t, 0)] == c0
+        # the finisher adds the pieces of pairs c0 .. f-1, each holding this tile's piece
+        for c in range(c0, f):
+            assert nonfinishing.get(c) == t
+    # every unfinished piece is added by the finisher of its tile
+    for c, t in nonfinishing.items():
+        assert capi.sk_owner(t * k_blocks, items, G) <= c < finisher[t]
+
+
+@pytest.mark.parametrize("sk_tiles,k_blocks,pairs", [
+    (34, 64, 74),      # 4096^3 on 256 x 256 tiles: 222 whole tiles + 34 in the tail
+    (22, 64, 74),      # 8192 x 6144 x 4096
+    (73, 128, 74), (1, 128, 74), (1, 1, 74), (3, 2, 74), (5, 30, 8), (7, 3, 8),
+    (2, 1000, 3), (9, 17, 74), (60, 5, 74),
+])
+def test_stream_k_split_covers_every_item_once_with_one_piece_per_pair(sk_tiles, k_blocks, pairs):
+    _check_stream_k_split(sk_tiles, k_blocks, pairs)
+
+
+def test_stream_k_split_random_shapes():
+    import random
+    rng = random.Random(7)
+    for _ in range(300):
+        pairs = rng.choice([74, 70, 37, 8, 2])
+        _check_stream_k_split(rng.randint(1, pairs), rng.randint(1, 300), pairs)
