@@ -1232,17 +1232,28 @@ int run_gemm_host(const void* A, const void* B, void* C, int M, int N, int K, in
       for (int i = 0; ok && i <= s2 && i < mb; ++i) ok = issue(i, s2);
     }
   }
-  // Join: the download stream follows the other two, frees the buffers and
-  // releases the caller's stream.
-  if (ok)
-    ok = cudaEventRecord(ev_start, p->up) == cudaSuccess &&
-         cudaStreamWaitEvent(p->down, ev_start, 0) == cudaSuccess &&
-         cudaEventRecord(ev_mm[pairs - 1], p->mm) == cudaSuccess &&
-         cudaStreamWaitEvent(p->down, ev_mm[pairs - 1], 0) == cudaSuccess;
+  // Join, after an error too (work already queued may still use the device
+  // buffers and the caller's host memory): the download stream follows the
+  // other two, frees the buffers and releases the caller's stream.  Where an
+  // ordering step itself fails, the pipeline's streams are drained instead,
+  // so nothing of this call is in flight when it returns an error.
+  const bool joined = cudaEventRecord(ev_start, p->up) == cudaSuccess &&
+                      cudaStreamWaitEvent(p->down, ev_start, 0) == cudaSuccess &&
+                      cudaEventRecord(ev_mm[pairs - 1], p->mm) == cudaSuccess &&
+                      cudaStreamWaitEvent(p->down, ev_mm[pairs - 1], 0) == cudaSuccess;
+  if (!joined) {
+    cudaGetLastError();
+    cudaStreamSynchronize(p->up);
+    cudaStreamSynchronize(p->mm);
+  }
   cudaFreeAsync(ws, p->down);
-  ok = ok && cudaEventRecord(ev_end, p->down) == cudaSuccess &&
-       cudaStreamWaitEvent(stream, ev_end, 0) == cudaSuccess;
-  return finish(ok ? B200_OK : B200_ERR_LAUNCH);
+  const bool released = cudaEventRecord(ev_end, p->down) == cudaSuccess &&
+                        cudaStreamWaitEvent(stream, ev_end, 0) == cudaSuccess;
+  if (!released) {
+    cudaGetLastError();
+    cudaStreamSynchronize(p->down);
+  }
+  return finish(ok && joined && released ? B200_OK : B200_ERR_LAUNCH);
 }
 
 // ---------------------------------------------------------------------------
