@@ -114,10 +114,15 @@ class FusedKSplit:
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.comm, handle = capi.ksplit_create(self.rank, self.world, max_m, max_n)
         handles = [handle]
-        if self.collective:
-            handles = [None] * self.world
-            dist.all_gather_object(handles, handle, group=group)
-        capi.ksplit_connect(self.comm, b"".join(handles))
+        try:
+            if self.collective:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, handle, group=group)
+            capi.ksplit_connect(self.comm, b"".join(handles))
+        except BaseException:
+            capi.ksplit_destroy(self.comm)       # unmaps what was mapped, frees the area
+            self.comm = None
+            raise
         if self.collective:
             dist.barrier(group)
 
@@ -129,17 +134,37 @@ class FusedKSplit:
 
         if self.comm is None:
             raise RuntimeError("FusedKSplit is closed")
+        self._check_operands(A_k, Bt_k)
         M, K = A_k.shape
         N = Bt_k.shape[0]
-        if not (A_k.is_contiguous() and Bt_k.is_contiguous()) or Bt_k.shape[1] != K:
-            raise ValueError("A_k (M x K_r) and Bt_k (N x K_r) must be contiguous")
         if out is None:
             out = torch.empty(M // self.world, N, dtype=torch.bfloat16, device=A_k.device)
+        else:
+            self._check_out(out, M, N, A_k.device)
         st = capi.ksplit_gemm_bf16(self.comm, A_k.data_ptr(), Bt_k.data_ptr(), out.data_ptr(),
                                    M, N, K, K, K, out.stride(0),
                                    torch.cuda.current_stream(A_k.device).cuda_stream)
         capi.check(st, "b200_ksplit_gemm_bf16")
         return out
+
+    @staticmethod
+    def _check_operands(A_k: torch.Tensor, Bt_k: torch.Tensor) -> None:
+        if A_k.dim() != 2 or Bt_k.dim() != 2 or Bt_k.shape[1] != A_k.shape[1]:
+            raise ValueError("A_k must be M x K_r and Bt_k N x K_r")
+        if A_k.dtype != torch.bfloat16 or Bt_k.dtype != torch.bfloat16:
+            raise TypeError("A_k and Bt_k must be bfloat16")
+        if A_k.device != Bt_k.device or A_k.device.type != "cuda":
+            raise ValueError("A_k and Bt_k must be on this rank's GPU")
+        if not (A_k.is_contiguous() and Bt_k.is_contiguous()):
+            raise ValueError("A_k (M x K_r) and Bt_k (N x K_r) must be contiguous")
+
+    def _check_out(self, out: torch.Tensor, M: int, N: int, device: torch.device) -> None:
+        # The kernel writes M/P rows of N columns at out's row stride: a
+        # smaller or differently typed buffer would be written past its end.
+        if out.dtype != torch.bfloat16 or out.device != device:
+            raise TypeError("out must be bfloat16 on the operands' GPU")
+        if tuple(out.shape) != (M // self.world, N) or out.stride(1) != 1:
+            raise ValueError(f"out must be ({M // self.world}, {N}) with unit column stride")
 
     def close(self) -> None:
         from . import capi

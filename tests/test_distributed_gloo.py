@@ -114,3 +114,28 @@ def test_slicing_rules():
     assert bdist.k_slice(8, 2, 1) == slice(4, 8)
     with pytest.raises(ValueError):
         bdist.k_slice(9, 2, 0)
+
+
+def test_fused_k_split_checks_operands_and_out_before_any_call():
+    # The checks run before the C ABI is reached, so an instance whose
+    # construction (a device collective) is skipped can exercise them.
+    from blackwell_gemm_b200.distributed import FusedKSplit
+
+    fk = object.__new__(FusedKSplit)
+    fk.world = 2
+    A = torch.zeros(512, 64, dtype=torch.bfloat16)
+    B = torch.zeros(256, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):                 # CPU tensors are not on a GPU
+        fk._check_operands(A, B)
+    with pytest.raises(TypeError):
+        fk._check_operands(A.float(), B)
+    with pytest.raises(ValueError):
+        fk._check_operands(A, B[:, :32])
+    dev = torch.device("cpu")
+    fk._check_out(torch.empty(256, 256, dtype=torch.bfloat16), 512, 256, dev)
+    with pytest.raises(ValueError):                 # too few rows for M / P
+        fk._check_out(torch.empty(128, 256, dtype=torch.bfloat16), 512, 256, dev)
+    with pytest.raises(ValueError):                 # columns not contiguous
+        fk._check_out(torch.empty(256, 512, dtype=torch.bfloat16)[:, ::2], 512, 256, dev)
+    with pytest.raises(TypeError):
+        fk._check_out(torch.empty(256, 256, dtype=torch.float32), 512, 256, dev)
