@@ -201,12 +201,23 @@ def gemm_ours(A, Bt, C, stream):
         raise RuntimeError(f"b200_gemm_bf16 failed: {capi.status_string(st)}")
 
 
-def gemm_reference(A, Bt, C, stream):
-    """The reference's own matmul_v8, through its launcher (legacy stream)."""
+def gemm_reference(A, Bt, C, stream, version="v8"):
+    """The reference's own matmul_<version> (v8 by default), through its
+    launcher (legacy stream)."""
     import oracle
     M, K = A.shape
     N = Bt.shape[0]
-    oracle.ref_gemm("v8", A.data_ptr(), Bt.data_ptr(), C.data_ptr(), M, N, K)
+    oracle.ref_gemm(version, A.data_ptr(), Bt.data_ptr(), C.data_ptr(), M, N, K)
+
+
+# Versions of the reference timed as its "best version" baseline: every
+# launcher its binding exports (src/matmul.cpp:4-13), where the shape allows.
+REFERENCE_VERSIONS = ["v1_2d", "v1_3d", "v2", "v3", "v4", "v5", "v6", "v7", "v8"]
+
+
+def reference_versions(M, N, K):
+    import oracle
+    return [v for v in REFERENCE_VERSIONS if oracle.ref_supports(v, M, N, K)]
 
 
 def parity_sample(C, A, Bt, nrows=256, seed=1):
@@ -366,6 +377,9 @@ def main():
                          "ksplit: 8192 x 8192 x 131072 with K split across the GPUs, "
                          "reduced inside the GEMM kernel over NVLink; "
                          "sweep: every single-GPU configuration shape, one line each")
+    ap.add_argument("--ref-versions", choices=["all", "v8", "none"], default="all",
+                    help="with --mode sweep: reference versions timed per shape (all that "
+                         "support it -- the best is reported --, v8 only, or none)")
     ap.add_argument("--shapes", default="",
                     help="with --mode sweep: comma-separated MxNxK shapes to time instead "
                          "of the configuration shapes (weights N(0, 0.02) for M <= 256, "
@@ -481,24 +495,31 @@ def main():
 
     extras = {}
     if rank == 0 and world == 1 and not args.no_extras:
-        ref_ms = None
+        ref_ms = {}
         try:
-            import oracle
             Cr = torch.empty_like(C)
-            if oracle.ref_supports("v8", M, N, K):
-                ref_ms = statistics.median(time_cold(lambda: gemm_reference(A, Bt, Cr, stream),
-                                                     50, 10, stream, flush))
+            for v in reference_versions(M, N, K):
+                ref_ms[v] = statistics.median(time_cold(
+                    lambda: gemm_reference(A, Bt, Cr, stream, v), 50, 10, stream, flush))
         except Exception as e:  # the reference build may be absent
-            extras["reference_v8_error"] = repr(e)
+            extras["reference_error"] = repr(e)
         cub_ms = statistics.median(time_cold(lambda: torch.matmul(A, Bt.T), 50, 10, stream, flush))
         ours_med = statistics.median(time_cold(lambda: gemm_ours(A, Bt, C, stream), 50, 10, stream,
                                                flush))
+        tf = lambda ms: flops_step / (ms * 1e-3) / 1e12
+        best = min(ref_ms, key=ref_ms.get) if ref_ms else None
         extras["baselines"] = {
-            "ours_median_tflops": flops_step / (ours_med * 1e-3) / 1e12,
-            "cublas_median_tflops": flops_step / (cub_ms * 1e-3) / 1e12,
-            "reference_v8_median_tflops": (flops_step / (ref_ms * 1e-3) / 1e12) if ref_ms else None,
+            "ours_median_tflops": tf(ours_med),
+            "cublas_median_tflops": tf(cub_ms),
+            "reference_v8_median_tflops": tf(ref_ms["v8"]) if "v8" in ref_ms else None,
+            "reference_versions_median_tflops": {v: tf(t) for v, t in ref_ms.items()},
+            "reference_best": {"version": best, "median_tflops": tf(ref_ms[best])} if best else None,
+            "ours_vs_cublas": cub_ms / ours_med,
+            "ours_vs_reference_best": (ref_ms[best] / ours_med) if best else None,
             "method": "median of 50 cold-L2 launches each after 1 s idle and 10 warm-up "
-                      "launches, same process and inputs (src/bench_core.py:47-69 method)"}
+                      "launches, same process and inputs (src/bench_core.py:47-69 method); "
+                      "every reference version that supports the shape "
+                      "(src/main.py:154-158 times each)"}
         extras["cpu_baseline"] = cpu_baseline(Bt)
 
     if rank == 0:
@@ -526,10 +547,180 @@ def main():
                        "smem_bytes": shape["smem_bytes"], "tuning": tuning},
         }
         line.update(extras)
+    # Per-rank spread of the headline: each rank's median step time and
+    # median SM clock name the slowest rank that sets the max over ranks.
+    mine = {"rank": rank, "median_ms": statistics.median(launch_ms),
+            "sm_mhz": clocks.report()["sm_mhz"]}
+    per_rank = [mine]
+    if world > 1:
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, mine)
+    # The two large multi-GPU configurations, measured at every N (N = 1
+    # included, so the lines of a scaling run give their curves).
+    more = {}
+    if not args.no_extras:
+        del C
+        torch.cuda.empty_cache()
+        more["m_shard_131072"] = extra_m_shard(args, world, rank, dev, Bt, flush, stream)
+        torch.cuda.empty_cache()
+        more["ksplit"] = extra_ksplit(args, world, rank, dev, flush, stream)
+    if rank == 0:
+        line["per_rank"] = per_rank
+        line.update(more)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def extra_steps(args) -> int:
+    """Timed steps of the side measurements: at most 20, at least 5."""
+    return max(5, min(args.steps, 20))
+
+
+def max_over_ranks(values, world, dev):
+    """Element-wise max over ranks of a list of floats."""
+    t = torch.tensor(values, dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
+def timed_cold_steps(step, steps, warmup, stream, flush, world):
+    """Cold-L2 steps between barriers: warm-up, then `steps` steps each
+    bracketed by CUDA events on `stream`.  Returns this rank's per-step ms."""
+    import torch.distributed as dist
+    step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    time.sleep(IDLE_BEFORE_ARM_S)
+    for _ in range(warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    starts, ends = cold_l2_loop(step, steps, stream, flush)
+    wait_event(ends[-1])
+    if world > 1:
+        dist.barrier()
+    return [a.elapsed_time(b) for a, b in zip(starts, ends)]
+
+
+def extra_m_shard(args, world, rank, dev, Bt, flush, stream):
+    """Configuration 5a as stated: M = 131072 rows in total, split over the N
+    ranks (strong scaling: rank r owns 131072 / N rows of A, B replicated, no
+    collective).  Value = all ranks' FLOPs / the slowest rank's summed GEMM
+    time.  At N > 1 rank 0 also times the whole 131072-row problem alone in
+    the same job (the 1-GPU point of the curve), and the line gives the
+    strong-scaling efficiency against it.  Parity on sampled rows of every
+    rank (max of the metrics over ranks)."""
+    from blackwell_gemm_b200 import parity as par_mod
+    from blackwell_gemm_b200.workloads import M_SHARD, make_operands
+    M, N, K = M_SHARD
+    rows = M // world
+    steps = extra_steps(args)
+    A, _ = make_operands(rows, 8, K, seed=5000 + rank, device=dev)
+    C = torch.empty(rows, N, dtype=torch.bfloat16, device=dev)
+    ms = timed_cold_steps(lambda: gemm_ours(A, Bt, C, stream), steps, 3, stream, flush, world)
+    par = parity_sample(C, A, Bt)
+    total, mx_scaled, mx_fro, fail = max_over_ranks(
+        [sum(ms), par["max_scaled"], par["rel_fro"], 0.0 if par["pass"] else 1.0], world, dev)
+    flops = 2 * M * N * K
+    out = {"value": flops * steps / (total * 1e-3) / 1e12, "unit": "TFLOP/s",
+           "ms_per_step": total / steps, "steps": steps, "scaling": "strong",
+           "config": {"M": M, "N": N, "K": K, "rows_per_gpu": rows,
+                      "inputs": "A (each rank's rows), B iid N(0,1) bf16, seeded, resident in HBM",
+                      "l2": "flushed: 256 MB written before every step"},
+           "parity": {"max_scaled": mx_scaled, "rel_fro": mx_fro, "pass": fail == 0.0,
+                      "rows_checked": 256 * world, "combined": "max over ranks"}}
+    del A, C
+    if world > 1:
+        import torch.distributed as dist
+        one = torch.zeros(1, dtype=torch.float64, device=dev)
+        if rank == 0:
+            # the whole problem on one GPU, in the same job (others wait)
+            torch.cuda.empty_cache()
+            Af, _ = make_operands(M, 8, K, seed=5000, device=dev)
+            Cf = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            s1 = max(3, steps // 4)
+            ms1 = timed_cold_steps(lambda: gemm_ours(Af, Bt, Cf, stream), s1, 3, stream, flush, 1)
+            one[0] = flops * s1 / (sum(ms1) * 1e-3) / 1e12
+            del Af, Cf
+        dist.barrier()
+        dist.broadcast(one, 0)
+        out["one_gpu_same_job"] = {"value": float(one[0]), "unit": "TFLOP/s",
+                                   "what": "rank 0 alone on all 131072 rows, same job"}
+        out["strong_scaling_efficiency"] = out["value"] / (world * float(one[0]))
+    return out
+
+
+def extra_ksplit(args, world, rank, dev, flush, stream):
+    """Configuration 5b: C = A B^T with M = N = 8192 and K = 131072 split over
+    the N ranks (strong scaling).  The fused kernel (b200_ksplit_gemm_bf16:
+    the other owners' fp32 tiles written into their memory over NVLink while
+    the GEMM runs, own rows summed and rounded in the epilogue) is timed
+    beside the unfused sequence (b200_gemm_bf16_f32out, NCCL
+    reduce_scatter_tensor(sum), b200_cast_f32_bf16), same inputs, cold L2,
+    max over ranks.  Parity of the fused output on sampled rows of every
+    owner against an fp32 GEMM over the whole K (distributed.
+    k_split_sampled_parity), and the device error word after the calls."""
+    import torch.distributed as dist
+    from blackwell_gemm_b200 import capi
+    from blackwell_gemm_b200 import distributed as bdist
+    from blackwell_gemm_b200.workloads import K_SPLIT, make_operands
+    M, N, K = K_SPLIT
+    Kr = K // world
+    steps = extra_steps(args)
+    group = dist.group.WORLD if world > 1 else None
+    A, _ = make_operands(M, 8, Kr, seed=2000 + rank, device=dev)
+    _, Bk = make_operands(8, N, Kr, seed=3000 + rank, device=dev)
+    fused = bdist.FusedKSplit(M, N, group)
+    out = torch.empty(M // world, N, dtype=torch.bfloat16, device=dev)
+    try:
+        def step_fused():
+            fused(A, Bk, out)
+
+        def step_unfused():
+            partial = bdist.gemm_f32_cuda(A, Bk)
+            if world > 1:
+                rs = torch.empty(M // world, N, dtype=torch.float32, device=dev)
+                dist.reduce_scatter_tensor(rs, partial, op=dist.ReduceOp.SUM, group=group)
+            else:
+                rs = partial
+            return bdist.cast_bf16_cuda(rs)
+
+        ms_unf = timed_cold_steps(step_unfused, steps, 3, stream, flush, world)
+        ms_fused = timed_cold_steps(step_fused, steps, 3, stream, flush, world)
+        torch.cuda.synchronize()
+        status = capi.device_status(True)
+        fused(A, Bk, out)        # a fresh result for the parity check
+        torch.cuda.synchronize()
+        par = bdist.k_split_sampled_parity(out, A, Bk, group)
+        status2 = capi.device_status(True)
+    finally:
+        torch.cuda.synchronize()
+        fused.close()
+    t_fused, t_unf, st = max_over_ranks([sum(ms_fused), sum(ms_unf), float(max(status, status2))],
+                                        world, dev)
+    flops = 2 * M * N * K
+    tf = lambda t: flops * steps / (t * 1e-3) / 1e12
+    return {"value": tf(t_fused), "unit": "TFLOP/s", "ms_per_step": t_fused / steps,
+            "steps": steps, "scaling": "strong",
+            "config": {"M": M, "N": N, "K": K, "k_per_gpu": Kr,
+                       "inputs": "each rank's K-slices of A and B, iid N(0,1) bf16, seeded",
+                       "l2": "flushed: 256 MB written before every step"},
+            "path": "b200_ksplit_gemm_bf16: one kernel per rank, peers' fp32 tiles over "
+                    "NVLink (CUDA IPC, plain stores), own rows summed and rounded once",
+            "unfused_nccl": {"value": tf(t_unf), "ms_per_step": t_unf / steps,
+                             "what": "b200_gemm_bf16_f32out + NCCL reduce_scatter_tensor(sum) "
+                                     "+ b200_cast_f32_bf16" if world > 1 else
+                                     "b200_gemm_bf16_f32out + b200_cast_f32_bf16 (one rank)"},
+            "fused_vs_unfused": t_unf / t_fused,
+            "nvlink_bytes_per_rank_per_step": (world - 1) * (M // world) * N * 4,
+            "device_status": int(st), "parity": par}
 
 
 def run_ksplit(args, world, rank, dev):
@@ -671,13 +862,19 @@ def run_sweep(args, world, rank, dev):
             med = lambda fn: statistics.median(time_cold(fn, steps, args.warmup, stream, flush))
             ours = med(lambda: gemm_ours(A, Bt, C, stream))
             cub = med(lambda: torch.matmul(A, Bt.T))
-            ref = None
-            try:
-                if oracle.ref_supports("v8", M, N, K):
-                    Cr = torch.empty_like(C)
-                    ref = med(lambda: gemm_reference(A, Bt, Cr, stream))
-            except Exception:
-                ref = None
+            refs = {}
+            if args.ref_versions != "none":
+                want = reference_versions(M, N, K)
+                if args.ref_versions == "v8":
+                    want = [v for v in want if v == "v8"]
+                Cr = torch.empty_like(C)
+                for v in want:
+                    try:
+                        refs[v] = med(lambda: gemm_reference(A, Bt, Cr, stream, v))
+                    except Exception:
+                        pass
+            best = min(refs, key=refs.get) if refs else None
+            ref = refs.get(best)
             fl = workloads.flops(M, N, K)
             by = workloads.min_bytes(M, N, K)
             tf = lambda ms: fl / (ms * 1e-3) / 1e12
@@ -686,8 +883,12 @@ def run_sweep(args, world, rank, dev):
             print(json.dumps({
                 "config": name, "M": M, "N": N, "K": K, "ours_us": ours * 1e3,
                 "ours_tflops": tf(ours), "cublas_tflops": tf(cub),
-                "reference_v8_tflops": tf(ref) if ref else None,
-                "ours_vs_cublas": cub / ours, "ours_vs_reference": (ref / ours) if ref else None,
+                "reference_v8_tflops": tf(refs["v8"]) if "v8" in refs else None,
+                "reference_best": {"version": best, "tflops": tf(ref)} if ref else None,
+                "reference_versions_tflops": {v: tf(t) for v, t in refs.items()},
+                "ours_vs_cublas": cub / ours,
+                "ours_vs_reference_v8": (refs["v8"] / ours) if "v8" in refs else None,
+                "ours_vs_reference_best": (ref / ours) if ref else None,
                 "roofline": {"bound": "hbm" if hbm else "tensor", "achieved": achieved,
                              "peak": peak_gbs if hbm else peak_tf,
                              "unit": "GB/s" if hbm else "TFLOP/s",
@@ -702,20 +903,36 @@ def run_reference(args, world, rank, dev):
     """The reference's own implementation of the path: its matmul_v8 kernel
     (src/kernels/kernel_v8.cu:830-833), built from its sources into
     oracle/_ref by oracle/build.py and called through its launcher.  The
-    reference has no CPU implementation; this GPU kernel is it.  Rank 0 alone
-    runs (single-GPU reference); other ranks exit without work."""
-    if rank != 0:
-        return
+    reference has no CPU implementation; this GPU kernel is it.  It is
+    single-GPU, so it runs one process per GPU (its tile-table cache is
+    device-blind, kernel_v8.cu:796-820): under torchrun every rank runs it on
+    its own 8192-row block of A with the replicated B -- the same row-sharded
+    workload and seeds as our arm -- and the per-rank summed GEMM time is
+    maxed over ranks, as for our arm, so the two lines compare like for like
+    at every N.  Rank 0 prints the line."""
+    import torch.distributed as dist
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     try:
         import oracle
         oracle.ref_lib()
+        missing = None
     except Exception as e:
-        print(json.dumps({"impl": "reference",
-                          "unavailable": f"reference build oracle/_ref missing: {e}"}))
+        missing = f"reference build oracle/_ref missing: {e}"
+    flag = torch.tensor([1.0 if missing else 0.0], device=dev)
+    if world > 1:
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+    if float(flag[0]) > 0:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": missing or
+                              "reference build missing on another rank"}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
         return
     from blackwell_gemm_b200.workloads import make_operands
     M, N, K = M_PER_GPU, N_DIM, K_DIM
-    A, _ = make_operands(M, 8, K, seed=1000, device=dev)
+    A, _ = make_operands(M, 8, K, seed=1000 + rank, device=dev)
     _, Bt = make_operands(8, N, K, seed=0, device=dev)
     C = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
@@ -729,40 +946,63 @@ def run_reference(args, world, rank, dev):
         flush.zero_()
         gemm_reference(A, Bt, C, stream)
     clocks = ClockSampler(dev.index)
+    if world > 1:
+        dist.barrier()
     torch.cuda.synchronize()
     clocks.start()
     starts, ends = cold_l2_loop(lambda: gemm_reference(A, Bt, C, stream), args.steps, stream,
                                 flush)
     wait_event(ends[-1])
+    if world > 1:
+        dist.barrier()
     clocks.stop()
     launch_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
-    total = sum(launch_ms)
     flops_step = 2 * M * N * K
-    value = flops_step * args.steps / (total * 1e-3) / 1e12
     e_ms, h2d, d2h = e2e_measure(gemm_reference, A, Bt, stream)
-    line = {
-        "metric": "BF16 GEMM TFLOP/s (cold-L2) at 8192^3 per GPU",
-        "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": total / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "bf16 GEMM C = A B^T, 8192 x 8192 x 8192 per GPU "
-                               "(reference runs on rank 0 only)",
-                   "M": M, "N": N, "K": K,
-                   "l2": "flushed: 256 MB written before every step, outside the GEMM events",
-                   "parallelism": "single GPU"},
-        "impl": "reference",
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": 0, "kind": "reference",
-                         "sample": "the reference's matmul_v8 GPU kernel on the full workload "
-                                   "(the reference has no CPU implementation of the path)"},
-        "e2e": {"value": flops_step / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e_ms,
-                "path": "reference matmul_v8 launcher with pinned host A, B and C"},
-        "gpu_launches": 0,
-        "step_ms": step_stats(launch_ms),
-        "clocks": clocks.report(),
-        "parity": par,
-    }
-    print(json.dumps(line), flush=True)
+    total, e_max, mx_scaled, mx_fro, fail = max_over_ranks(
+        [sum(launch_ms), e_ms, par["max_scaled"], par["rel_fro"], 0.0 if par["pass"] else 1.0],
+        world, dev)
+    mine = {"rank": rank, "median_ms": statistics.median(launch_ms),
+            "sm_mhz": clocks.report()["sm_mhz"]}
+    per_rank = [mine]
+    if world > 1:
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, mine)
+    value = flops_step * world * args.steps / (total * 1e-3) / 1e12
+    if rank == 0:
+        line = {
+            "metric": "BF16 GEMM TFLOP/s (cold-L2) at 8192^3 per GPU",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "bf16 GEMM C = A B^T, 8192 x 8192 x 8192 per GPU "
+                                   "(rows of A sharded, B replicated, no collective; the "
+                                   "reference's v8 in one process per GPU)",
+                       "M": M * world, "N": N, "K": K, "m_per_gpu": M,
+                       "inputs": "A, B iid N(0,1) bf16, seeded, resident in HBM",
+                       "l2": "flushed: 256 MB written before every step, outside the GEMM events",
+                       "parallelism": f"m-shard{world}"},
+            "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": 0, "kind": "reference",
+                             "sample": "the reference's matmul_v8 GPU kernel on the full "
+                                       "workload (the reference has no CPU implementation of "
+                                       "the path)"},
+            "e2e": {"value": flops_step * world / (e_max * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                    "ms_per_step": e_max,
+                    "path": "reference matmul_v8 launcher with pinned host A, B and C, serial "
+                            "copies, every rank (max over ranks)"},
+            "gpu_launches": 0,
+            "step_ms": step_stats(launch_ms),
+            "per_rank": per_rank,
+            "clocks": clocks.report(),
+            "parity": {"max_scaled": mx_scaled, "rel_fro": mx_fro, "pass": fail == 0.0,
+                       "rows_checked": 256 * world, "combined": "max over ranks"},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -44,6 +44,8 @@ SIGNATURES = {
     "b200_gemm_bf16_profile": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp]),
     "b200_gemm_bf16_f32out": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "b200_gemm_bf16_noalloc": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "b200_gemm_noalloc_status": (_i, [_i, _ip]),
+    "b200_gemm_noalloc_wait_probe": (_i, [_ull, _vp]),
     "b200_cast_f32_bf16": (_i, [_vp, _i, _vp, _i, _i, _i, _vp]),
     "b200_gemm_bf16_host": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "b200_gemm_bf16_epilogue": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, ctypes.c_float, _vp,
@@ -144,8 +146,22 @@ def cast_f32_bf16(w_ptr: int, ldw: int, c_ptr: int, ldc: int, M: int, N: int,
 def gemm_bf16_noalloc(a_ptr: int, b_ptr: int, c_ptr: int, M: int, N: int, K: int, lda: int,
                       ldb: int, ldc: int, stream: int = 0) -> int:
     """b200_gemm_bf16 without any device allocation (fixed 16 MiB scratch in
-    the library; overlapping calls race).  Returns the status."""
+    the library; overlapping calls race; timeouts are read with
+    noalloc_status).  Returns the status."""
     return lib().b200_gemm_bf16_noalloc(a_ptr, b_ptr, c_ptr, M, N, K, lda, ldb, ldc, stream)
+
+
+def noalloc_status(clear: bool = True) -> int:
+    """Error word of the allocation-free entry point's array (sticky until
+    cleared); synchronises the device."""
+    v = ctypes.c_int(0)
+    check(lib().b200_gemm_noalloc_status(1 if clear else 0, ctypes.byref(v)), "noalloc_status")
+    return v.value
+
+
+def noalloc_wait_probe(timeout_ns: int, stream: int = 0) -> int:
+    """The wait self-test, recording into the allocation-free array's word."""
+    return lib().b200_gemm_noalloc_wait_probe(int(timeout_ns), stream)
 
 
 def set_splits(splits: int) -> None:

@@ -351,6 +351,21 @@ int device_state(DeviceState** out) {
 
 long long ceil_div(long long a, long long b) { return (a + b - 1) / b; }
 
+// Scratch memory given to a call instead of the device's pool (the
+// allocation-free entry point passes its fixed array).  flags: a region that
+// holds only epoch flags, so values left there by earlier calls are always
+// older epochs; epoch: the value this call's flags are raised to (each call
+// takes a new one), or 0 under stream capture, where the used flags are
+// cleared on the stream and the call raises them to 1.  work: workspaces
+// (fp32 split-K accumulators, stream-K slots), reused by every call.
+struct Scratch {
+  unsigned int* flags = nullptr;
+  size_t flag_count = 0;
+  unsigned int epoch = 0;
+  char* work = nullptr;
+  size_t work_bytes = 0;
+};
+
 // Fraction of pair-slots doing useful work over the persistent waves.
 double wave_efficiency(long long tiles, int pairs) {
   const long long waves = ceil_div(tiles, pairs);
@@ -519,10 +534,11 @@ unsigned int* stream_flags(cudaStream_t stream, size_t count, unsigned int* epoc
   if (g_num_stream_flags == kMaxStreamFlags) return nullptr;
   const size_t n = count < 4096 ? 4096 : count;
   unsigned int* p = nullptr;
-  // cudaMalloc + a blocking clear, once per stream: the array starts at epoch 0.
+  // Once per (device, stream): cudaMalloc, then a clear queued on the stream
+  // itself -- every kernel that reads the array runs on that stream, after
+  // the clear, so nothing waits on the host or on other streams.
   if (cudaMalloc(&p, n * sizeof(unsigned int)) != cudaSuccess ||
-      cudaMemset(p, 0, n * sizeof(unsigned int)) != cudaSuccess ||
-      cudaDeviceSynchronize() != cudaSuccess) {
+      cudaMemsetAsync(p, 0, n * sizeof(unsigned int), stream) != cudaSuccess) {
     cudaGetLastError();
     if (p) cudaFree(p);
     return nullptr;
@@ -670,7 +686,8 @@ bool skinny_use_stream(int M, int N, int K) {
 
 template <int kMp, int kSlabsWanted>
 int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
-                  int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi) {
+                  int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi,
+                  const Scratch* scratch) {
   constexpr int kTiles = skinny_tiles(kMp);
   constexpr int kSlabs = skinny_fit_slabs(kMp, kSlabsWanted, kTiles);
   using P = SkinnyCfg<kMp, kSlabs, kTiles>;
@@ -694,8 +711,11 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
   const int ldw = (int)ceil_div(N, 8) * 8;
   const size_t bytes = (size_t)M * ldw * sizeof(float);
   float* W = nullptr;
-  if (cudaMallocFromPoolAsync(reinterpret_cast<void**>(&W), bytes, d.pool, stream) !=
-      cudaSuccess) {
+  if (scratch != nullptr) {
+    if (bytes > scratch->work_bytes) return B200_ERR_TOO_LARGE;
+    W = reinterpret_cast<float*>(scratch->work);
+  } else if (cudaMallocFromPoolAsync(reinterpret_cast<void**>(&W), bytes, d.pool, stream) !=
+             cudaSuccess) {
     cudaGetLastError();
     return B200_ERR_LAUNCH;
   }
@@ -709,7 +729,7 @@ int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, in
     if (cudaGetLastError() != cudaSuccess) st = B200_ERR_LAUNCH;
   }
   if (st == B200_OK) st = cast_to_bf16(W, ldw, C, ldc, M, N, d.sms, stream, epi);
-  cudaFreeAsync(W, stream);
+  if (scratch == nullptr) cudaFreeAsync(W, stream);
   return st;
 }
 
@@ -722,7 +742,8 @@ long long stream_owner_host(long long x, long long total, int G) {
 
 template <int kMp, int kSlabs>
 int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, int K, int lda,
-                         int ldb, int ldc, DeviceState& d, cudaStream_t stream) {
+                         int ldb, int ldc, DeviceState& d, cudaStream_t stream,
+                         const Scratch* scratch) {
   using P = SkinnyCfg<kMp, kSlabs>;
   CUtensorMap tb, ta, tc;
   if (encode_2d(&tb, B, K, N, ldb, kSlabK, P::kRowsB) != B200_OK ||
@@ -748,32 +769,48 @@ int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, in
   args.max_seg = max_seg;
   args.status = d.status;
   args.timeout_ns = g_timeout_ns.load();
-  const size_t flag_bytes = (size_t)ceil_div((long long)args.tiles * max_seg * 4 * 4, 256) * 256;
+  const size_t nflags = (size_t)args.tiles * max_seg * 4;
+  const size_t flag_bytes = (size_t)ceil_div((long long)nflags * 4, 256) * 256;
   const size_t slot_bytes = (size_t)args.tiles * max_seg * kMp * P::kRowsB * sizeof(float);
   char* ws = nullptr;
-  if (cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), flag_bytes + slot_bytes, d.pool,
-                              stream) != cudaSuccess) {
-    cudaGetLastError();
-    return B200_ERR_LAUNCH;
-  }
-  args.slots = reinterpret_cast<float*>(ws + flag_bytes);
-  // Flags: the stream's epoch-numbered array outside capture (no clearing
-  // operation before the kernel), cleared workspace flags under capture.
   int st = B200_OK;
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
-    cudaGetLastError();
-    cap = cudaStreamCaptureStatusActive;
-  }
-  unsigned int* persistent = nullptr;
-  if (cap == cudaStreamCaptureStatusNone)
-    persistent = stream_flags(stream, (size_t)args.tiles * max_seg * 4, &args.epoch);
-  if (persistent != nullptr) {
-    args.flags = persistent;
+  if (scratch != nullptr) {
+    // The caller's scratch: slots in its workspace, flags in its flag region
+    // (a new epoch per call, or cleared flags under capture).
+    if (slot_bytes > scratch->work_bytes || nflags > scratch->flag_count)
+      return B200_ERR_TOO_LARGE;
+    args.slots = reinterpret_cast<float*>(scratch->work);
+    args.flags = scratch->flags;
+    args.epoch = scratch->epoch;
+    if (args.epoch == 0) {
+      args.epoch = 1;
+      if (cudaMemsetAsync(scratch->flags, 0, nflags * 4, stream) != cudaSuccess)
+        st = B200_ERR_LAUNCH;
+    }
   } else {
-    args.flags = reinterpret_cast<unsigned int*>(ws);
-    args.epoch = 1;
-    if (cudaMemsetAsync(ws, 0, flag_bytes, stream) != cudaSuccess) st = B200_ERR_LAUNCH;
+    if (cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), flag_bytes + slot_bytes, d.pool,
+                                stream) != cudaSuccess) {
+      cudaGetLastError();
+      return B200_ERR_LAUNCH;
+    }
+    args.slots = reinterpret_cast<float*>(ws + flag_bytes);
+    // Flags: the stream's epoch-numbered array outside capture (no clearing
+    // operation before the kernel), cleared workspace flags under capture.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+      cudaGetLastError();
+      cap = cudaStreamCaptureStatusActive;
+    }
+    unsigned int* persistent = nullptr;
+    if (cap == cudaStreamCaptureStatusNone)
+      persistent = stream_flags(stream, nflags, &args.epoch);
+    if (persistent != nullptr) {
+      args.flags = persistent;
+    } else {
+      args.flags = reinterpret_cast<unsigned int*>(ws);
+      args.epoch = 1;
+      if (cudaMemsetAsync(ws, 0, flag_bytes, stream) != cudaSuccess) st = B200_ERR_LAUNCH;
+    }
   }
   if (st == B200_OK) {
     // Cooperative: the fix-up waits on CTAs of higher index, so all G CTAs
@@ -794,15 +831,17 @@ int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, in
       st = B200_ERR_LAUNCH;
     }
   }
-  cudaFreeAsync(ws, stream);
+  if (ws != nullptr) cudaFreeAsync(ws, stream);
   return st;
 }
 
 template <int kSlabs>
 int run_skinny_stream_slabs(const void* A, const void* B, void* C, int M, int N, int K, int lda,
-                            int ldb, int ldc, DeviceState& d, cudaStream_t stream) {
-#define B200_SKS(MP) \
-  launch_skinny_stream<MP, skinny_fit_slabs(MP, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d, stream)
+                            int ldb, int ldc, DeviceState& d, cudaStream_t stream,
+                            const Scratch* scratch) {
+#define B200_SKS(MP)                                                                         \
+  launch_skinny_stream<MP, skinny_fit_slabs(MP, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d, \
+                                                         stream, scratch)
   if (M <= 16) return B200_SKS(16);
   if (M <= 32) return B200_SKS(32);
   if (M <= 64) return B200_SKS(64);
@@ -813,16 +852,16 @@ int run_skinny_stream_slabs(const void* A, const void* B, void* C, int M, int N,
 
 template <int kSlabs>
 int run_skinny_slabs(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
-                     int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi) {
-  if (M <= 16)
-    return launch_skinny<16, kSlabs>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
-  if (M <= 32)
-    return launch_skinny<32, kSlabs>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
-  if (M <= 64)
-    return launch_skinny<64, kSlabs>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
-  if (M <= 128)
-    return launch_skinny<128, kSlabs>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
-  return launch_skinny<256, kSlabs>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
+                     int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi,
+                     const Scratch* scratch) {
+#define B200_SKW(MP) \
+  launch_skinny<MP, kSlabs>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi, scratch)
+  if (M <= 16) return B200_SKW(16);
+  if (M <= 32) return B200_SKW(32);
+  if (M <= 64) return B200_SKW(64);
+  if (M <= 128) return B200_SKW(128);
+  return B200_SKW(256);
+#undef B200_SKW
 }
 
 // K slabs per stage of the skinny kernel (B200_GEMM_SKINNY_SLABS: 1, 2, 4).
@@ -908,7 +947,8 @@ int run_skinny_cluster(const void* A, const void* B, void* C, int M, int N, int 
 }
 
 int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
-               int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi = nullptr) {
+               int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi = nullptr,
+               const Scratch* scratch = nullptr) {
   // Per shape (mode 1): for the fewest rows of A (skinny_use_cluster) the
   // single-launch cluster kernel (A's box is then mostly out of bounds, so
   // nearly only B streams); up to 128 rows the stream-K kernel (all SMs, no
@@ -919,9 +959,9 @@ int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int l
   // (a forced slice count, b200_gemm_set_splits, takes the split-K kernels)
   if (epi == nullptr && (mode == 3 || (mode == 1 && skinny_use_stream(M, N, K)))) {
     switch (skinny_slabs()) {
-      case 1: return run_skinny_stream_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
-      case 4: return run_skinny_stream_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
-      default: return run_skinny_stream_slabs<2>(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
+      case 1: return run_skinny_stream_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, scratch);
+      case 4: return run_skinny_stream_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, scratch);
+      default: return run_skinny_stream_slabs<2>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, scratch);
     }
   }
   // (The cluster kernel writes C directly, so fused epilogues take the
@@ -929,9 +969,9 @@ int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int l
   if (epi == nullptr && (mode == 2 || skinny_use_cluster(M, N, K)))
     return run_skinny_cluster(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
   switch (skinny_slabs()) {
-    case 1: return run_skinny_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
-    case 4: return run_skinny_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
-    default: return run_skinny_slabs<2>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi);
+    case 1: return run_skinny_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi, scratch);
+    case 4: return run_skinny_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi, scratch);
+    default: return run_skinny_slabs<2>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi, scratch);
   }
 }
 
@@ -1685,14 +1725,24 @@ int b200_ksplit_destroy(b200_ksplit_comm* c) {
 // of its scratch in the fixed array below, which every GPU that loads this
 // library holds until exit.
 //
-// Layout of the scratch array: bytes [0, 256) hold the kernel's error word
-// (at offset 0), bytes [256, end) the split-K fp32 workspace, so a split-K
-// call fits when M * round_up(N, 8) * 4 <= kNoAllocWorkspaceBytes (16 MiB
-// minus 256 B: e.g. M up to 511 at N = 8192).
+// Layout of the scratch array (16 MiB):
+//   [0, 4)            error word of the kernels this entry point launches
+//                     (sticky: read and cleared by b200_gemm_noalloc_status)
+//   [256, 64 KiB)     epoch flags of the skinny stream-K kernel (only flags
+//                     live here, so values left by earlier calls are older
+//                     epochs and nothing needs clearing between calls)
+//   [64 KiB, 16 MiB)  workspace: split-K fp32 accumulators, stream-K slots
+// Split-K slice counts chosen per shape always fit (the pair kernel splits
+// only grids of at most ~600 K outputs, 2.4 MB of fp32; a skinny call whose
+// workspace would not fit runs the cluster kernel, which needs none); only a
+// forced slice count (b200_gemm_set_splits) can need more than the
+// workspace, and such a call returns B200_ERR_TOO_LARGE.
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 16u << 20;
-constexpr size_t kNoAllocWorkspaceOffset = 256;
+constexpr size_t kNoAllocFlagsOffset = 256;
+constexpr size_t kNoAllocWorkspaceOffset = 64u << 10;
+constexpr size_t kNoAllocFlagCount = (kNoAllocWorkspaceOffset - kNoAllocFlagsOffset) / 4;
 constexpr size_t kNoAllocWorkspaceBytes = kNoAllocScratchBytes - kNoAllocWorkspaceOffset;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
@@ -1700,31 +1750,41 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 struct NoAllocDevice {
   bool ready = false;
   int init_status = B200_OK;
-  DeviceState launch;           // sms and max_pairs only; status/pool stay unset
+  DeviceState launch;           // sms, max_pairs, sk_clusters; status = the array's error word
   unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
+  unsigned int epoch = 0;       // flag epochs handed out so far
 };
 
 std::mutex g_noalloc_mu;
 NoAllocDevice g_noalloc_dev[kMaxDevices];
 
 // Once per device, with that device current: the same architecture checks,
-// shared-memory limits and occupancy query as the allocating path, plus the
-// device address of the scratch array.  None of these calls allocate.
+// shared-memory limits and occupancy queries as the allocating path (which
+// also load every kernel this entry point launches), plus the device address
+// of the scratch array.  None of these calls allocate.
 int noalloc_setup(NoAllocDevice& nd, int dev) {
   cudaDeviceProp prop;
   if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return B200_ERR_UNSUPPORTED_DEVICE;
   if (prop.major != 10 || prop.minor != 0) return B200_ERR_UNSUPPORTED_DEVICE;
   if (encode_tiled() == nullptr) return B200_ERR_TENSOR_MAP;
   nd.launch.sms = prop.multiProcessorCount;
-  if (!set_smem_limit<false, kV256x64, kOutF32Add>()) return B200_ERR_LAUNCH;
+  if (!set_smem_limit<false, kV256x64, kOutF32Add>() || !set_skinny_limits())
+    return B200_ERR_LAUNCH;
   const int vst = init_variants(nd.launch.sms, nd.launch.max_pairs);
   if (vst != B200_OK) return vst;
-  // In host code g_noalloc_scratch names a host-side stand-in; the kernel
+  if (!skc_init_all(nd.launch)) return B200_ERR_LAUNCH;
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, cast_f32_to_bf16_kernel) != cudaSuccess ||
+      cudaFuncGetAttributes(&fa, wait_probe_kernel) != cudaSuccess)
+    return B200_ERR_LAUNCH;
+  // In host code g_noalloc_scratch names a host-side stand-in; the kernels
   // must be given the device address.
   void* p = nullptr;
   if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
     return B200_ERR_LAUNCH;
   nd.scratch = static_cast<unsigned char*>(p);
+  nd.launch.status = reinterpret_cast<int*>(nd.scratch);
+  nd.launch.pool = nullptr;
   return B200_OK;
 }
 
@@ -1747,6 +1807,31 @@ int noalloc_device(NoAllocDevice** out) {
   return B200_OK;
 }
 
+// The scratch of one call: a new flag epoch (2, 3, ...) outside stream
+// capture; under capture (a graph may be replayed with the same epoch) epoch
+// 0, which makes the skinny stream-K launch clear the flags it uses on the
+// stream and raise them to 1, below every epoch handed out here.  Flags are
+// compared by signed difference, so a wrap of the counter keeps older epochs
+// older.
+Scratch noalloc_scratch(NoAllocDevice& nd, cudaStream_t stream) {
+  Scratch sc;
+  sc.flags = reinterpret_cast<unsigned int*>(nd.scratch + kNoAllocFlagsOffset);
+  sc.flag_count = kNoAllocFlagCount;
+  sc.work = reinterpret_cast<char*>(nd.scratch + kNoAllocWorkspaceOffset);
+  sc.work_bytes = kNoAllocWorkspaceBytes;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+    cudaGetLastError();
+    cap = cudaStreamCaptureStatusActive;
+  }
+  if (cap == cudaStreamCaptureStatusNone) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (++nd.epoch < 2) nd.epoch = 2;
+    sc.epoch = nd.epoch;
+  }
+  return sc;
+}
+
 int run_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K, int lda,
                      int ldb, int ldc, cudaStream_t stream) {
   int st = validate(A, B, C, M, N, K, lda, ldb, ldc);
@@ -1759,6 +1844,16 @@ int run_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K,
     return cudaMemset2DAsync(C, (size_t)ldc * 2, 0, (size_t)N * 2, M, stream) == cudaSuccess
                ? B200_OK
                : B200_ERR_LAUNCH;
+  // Skinny M: the same per-shape kernel as the allocating path, its workspace
+  // (if any) in the array; where that does not fit, the cluster kernel, which
+  // adds its K slices in distributed shared memory and needs no workspace.
+  if (use_skinny(M, N, K)) {
+    const Scratch sc = noalloc_scratch(*nd, stream);
+    st = run_skinny(A, B, C, M, N, K, lda, ldb, ldc, nd->launch, stream, nullptr, &sc);
+    if (st == B200_ERR_TOO_LARGE)
+      st = run_skinny_cluster(A, B, C, M, N, K, lda, ldb, ldc, nd->launch, stream);
+    return st;
+  }
   const int splits =
       choose_splits(M, N, (int)ceil_div(K, kSlabK), nd->launch.max_pairs[kV256x64]);
   const int ldw = (int)ceil_div(N, 8) * 8;
@@ -1769,14 +1864,11 @@ int run_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K,
   if (encode_2d(&ta, A, K, M, lda, kSlabK, kCtaM) != B200_OK ||
       encode_2d(&tb, B, K, N, ldb, kSlabK, kCtaN) != B200_OK)
     return B200_ERR_TENSOR_MAP;
-  int* status = reinterpret_cast<int*>(nd->scratch);
-  float* W = reinterpret_cast<float*>(nd->scratch + kNoAllocWorkspaceOffset);
-  // The array keeps the previous call's contents: the error word and the
-  // split-K accumulator must start at zero.
-  if (cudaMemsetAsync(status, 0, sizeof(int), stream) != cudaSuccess) return B200_ERR_LAUNCH;
   GemmArgs args = base_args(M, N, K, nd->launch, nullptr, 0);
-  args.status = status;
   if (splits > 1) {
+    // The split-K accumulator must start at zero: the array keeps the
+    // previous call's contents.
+    float* W = reinterpret_cast<float*>(nd->scratch + kNoAllocWorkspaceOffset);
     if (encode_2d(&tc, W, N, M, ldw, 32, 32, true) != B200_OK) return B200_ERR_TENSOR_MAP;
     if (cudaMemsetAsync(W, 0, ws_bytes, stream) != cudaSuccess) return B200_ERR_LAUNCH;
     st = launch<false, kV256x64, kOutF32Add>(ta, tb, tc, args, splits, nd->launch, stream);
@@ -1784,7 +1876,8 @@ int run_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K,
     return cast_to_bf16(W, ldw, C, ldc, M, N, nd->launch.sms, stream);
   }
   if (encode_2d(&tc, C, N, M, ldc, kStoreCols, 32) != B200_OK) return B200_ERR_TENSOR_MAP;
-  // (no stream-K tail here: its workspace and flags would be allocations)
+  // (no stream-K tail here: its slots, 74 pairs x 8 pieces x 32 KiB, exceed
+  // the array's workspace)
   return launch_bf16<false>(choose_variant(M, N, nd->launch.max_pairs), ta, tb, tc, B, ldb, args,
                             nd->launch, stream, false);
 }
@@ -1794,4 +1887,28 @@ int run_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K,
 extern "C" int b200_gemm_bf16_noalloc(const void* A, const void* B, void* C, int M, int N,
                                       int K, int lda, int ldb, int ldc, void* stream) {
   return run_gemm_noalloc(A, B, C, M, N, K, lda, ldb, ldc, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b200_gemm_noalloc_status(int clear, int* status_out) {
+  if (!status_out) return B200_ERR_INVALID_ARGUMENT;
+  NoAllocDevice* nd = nullptr;
+  const int st = noalloc_device(&nd);
+  if (st != B200_OK) return st;
+  if (cudaDeviceSynchronize() != cudaSuccess) return B200_ERR_LAUNCH;
+  int v = 0;
+  if (cudaMemcpy(&v, nd->scratch, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return B200_ERR_LAUNCH;
+  if (clear && v != 0 && cudaMemset(nd->scratch, 0, sizeof(int)) != cudaSuccess)
+    return B200_ERR_LAUNCH;
+  *status_out = v;
+  return B200_OK;
+}
+
+extern "C" int b200_gemm_noalloc_wait_probe(unsigned long long timeout_ns, void* stream) {
+  if (timeout_ns == 0 || timeout_ns > 10000000000ull) return B200_ERR_INVALID_ARGUMENT;
+  NoAllocDevice* nd = nullptr;
+  const int st = noalloc_device(&nd);
+  if (st != B200_OK) return st;
+  wait_probe_kernel<<<2, 32, 0, static_cast<cudaStream_t>(stream)>>>(nd->launch.status, timeout_ns);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
 }

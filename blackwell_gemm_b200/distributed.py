@@ -147,14 +147,19 @@ class FusedKSplit:
         capi.check(st, "b200_ksplit_gemm_bf16")
         return out
 
-    @staticmethod
-    def _check_operands(A_k: torch.Tensor, Bt_k: torch.Tensor) -> None:
+    def _check_operands(self, A_k: torch.Tensor, Bt_k: torch.Tensor) -> None:
         if A_k.dim() != 2 or Bt_k.dim() != 2 or Bt_k.shape[1] != A_k.shape[1]:
             raise ValueError("A_k must be M x K_r and Bt_k N x K_r")
         if A_k.dtype != torch.bfloat16 or Bt_k.dtype != torch.bfloat16:
             raise TypeError("A_k and Bt_k must be bfloat16")
         if A_k.device != Bt_k.device or A_k.device.type != "cuda":
-            raise ValueError("A_k and Bt_k must be on this rank's GPU")
+            raise ValueError("A_k and Bt_k must be on one CUDA device")
+        if A_k.device != self.device:
+            # The communicator's receive area, its peer mappings and the
+            # kernel's launch belong to self.device: operands on another GPU
+            # must not reach the C ABI.
+            raise ValueError(f"A_k and Bt_k must be on this rank's GPU {self.device}, "
+                             f"not {A_k.device}")
         if not (A_k.is_contiguous() and Bt_k.is_contiguous()):
             raise ValueError("A_k (M x K_r) and Bt_k (N x K_r) must be contiguous")
 
@@ -184,3 +189,71 @@ def k_slice(K: int, world: int, rank: int) -> slice:
         raise ValueError(f"K={K} is not divisible by {world} ranks")
     k = K // world
     return slice(rank * k, (rank + 1) * k)
+
+
+def k_split_sampled_parity(out_rows: torch.Tensor, A_k: torch.Tensor, Bt_k: torch.Tensor,
+                           group: Optional[dist.ProcessGroup] = None, per_owner: int = 32,
+                           seed: int = 1) -> dict:
+    """Parity of a K-split GEMM's output against an fp32 GEMM of the same bf16
+    inputs over the WHOLE K, on sampled rows, although no rank holds all of K.
+
+    ``out_rows`` is this rank's (M/P, N) block of C; ``A_k`` (M x K_r) and
+    ``Bt_k`` (N x K_r) its K-slices.  Every rank draws the same ``per_owner``
+    rows from each owner's block, computes their fp32 partial over its own
+    K-slice (no TF32) together with the squared row norms of its slices, and
+    the partials and norms are summed across ranks (all_reduce), which gives
+    the full-K fp32 reference of the sampled rows and the full-K norms.  Each
+    rank then compares its own sampled rows; the metrics of ``parity.metrics``
+    are combined across ranks (max of ``max_scaled``; ``rel_fro`` over all
+    sampled rows).  A collective: every rank calls it.  Returns the same dict
+    on every rank."""
+    from . import parity
+
+    collective = dist.is_available() and dist.is_initialized()
+    world = dist.get_world_size(group) if collective else 1
+    rank = dist.get_rank(group) if collective else 0
+    M, N = A_k.shape[0], Bt_k.shape[0]
+    rows = M // world
+    if out_rows.shape[0] != rows or out_rows.shape[1] != N:
+        raise ValueError(f"out_rows must be ({rows}, {N})")
+    take = min(per_owner, rows)
+    g = torch.Generator().manual_seed(seed)
+    sample = torch.cat([q * rows + torch.randperm(rows, generator=g)[:take]
+                        for q in range(world)]).to(A_k.device)
+    a = A_k.index_select(0, sample)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = a.float() @ Bt_k.float().T                       # |S| x N partial over K_r
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    na2 = a.double().square().sum(1)
+    nb2 = Bt_k.double().square().sum(1)
+    if collective:
+        for t in (ref, na2, nb2):
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+    mine = slice(rank * take, (rank + 1) * take)
+    C = out_rows.index_select(0, sample[mine] - rank * rows).double()
+    R = ref[mine].double()
+    diff = (C - R).abs()
+    scale = na2[mine].sqrt()[:, None] * nb2.sqrt()[None, :]
+    ratio = torch.where(scale > 0, diff / scale.clamp_min(1e-300),
+                        torch.where(diff > 0, torch.full_like(diff, float("inf")),
+                                    torch.zeros_like(diff)))
+    finite = bool(torch.isfinite(C).all())
+    stats = torch.tensor([float(ratio.max()) if finite and ratio.numel() else
+                          (0.0 if finite else float("inf")),
+                          float(diff.square().sum()), float(R.square().sum())],
+                         dtype=torch.float64, device=A_k.device)
+    if collective:
+        mx = stats[:1].clone()
+        sums = stats[1:].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=group)
+        dist.all_reduce(sums, op=dist.ReduceOp.SUM, group=group)
+        stats = torch.cat([mx, sums])
+    max_scaled, sq_diff, sq_ref = (float(v) for v in stats)
+    rel_fro = (sq_diff / sq_ref) ** 0.5 if sq_ref > 0 else (0.0 if sq_diff == 0 else float("inf"))
+    m = {"max_scaled": max_scaled, "rel_fro": rel_fro}
+    return {**m, "pass": parity.passes(m), "rows_checked": take * world,
+            "against": "fp32 GEMM of the same bf16 inputs over the whole K (sampled rows; "
+                       "partials summed across ranks, no TF32)"}

@@ -107,7 +107,10 @@ int b200_gemm_set_skinny_mode(int mode);
  * the pair holding its last K blocks (fp32 pieces through a pool workspace,
  * one rounding).  0 = off, 1 = when the last wave would idle at least 3 % of
  * the pair-slots (default; B200_GEMM_STREAMK overrides), 2 = whenever the
- * last wave is partial.  No reference counterpart (the reference deals whole
+ * last wave is partial.  The first stream-K call (pair tail or skinny
+ * stream-K kernel) on each (device, stream) allocates that stream's flag
+ * array with cudaMalloc, which may synchronise the device; it is cleared on
+ * the stream itself.  No reference counterpart (the reference deals whole
  * tiles with cluster launch control). */
 int b200_gemm_set_stream_k(int mode);
 
@@ -168,22 +171,40 @@ const char* b200_gemm_status_string(int status);
  * break their accounting) and latency-critical loops in which
  * cudaMalloc/cudaFree would synchronize the device.  b200_gemm_bf16 allocates
  * on a device's first call (an error word and a split-K memory pool) and its
- * split-K calls draw workspaces from that pool; this entry point allocates
- * nothing.  Its scratch is one fixed 16 MiB device array in the library,
- * held by every GPU that loads the library until exit: a 4-byte error word
- * plus a split-K fp32 workspace of 16 MiB - 256 B.  A call that would split K
- * fits when M * round_up(N, 8) * 4 bytes <= 16 MiB - 256 B and otherwise
- * returns B200_ERR_TOO_LARGE; calls that do not split K use only the error
- * word, so every shape b200_gemm_bf16 runs without splitting runs here too.
- * Every call shares the array and clears the parts that must start at zero;
- * calls whose executions overlap on the GPU (other streams, other threads)
+ * split-K, skinny and stream-K calls draw workspaces from that pool; this
+ * entry point allocates nothing.  Its scratch is one fixed 16 MiB device
+ * array in the library, held by every GPU that loads the library until exit:
+ * a 4-byte error word, 64 KiB - 256 B of epoch flags and 16 MiB - 64 KiB of
+ * workspace (split-K fp32 accumulators, skinny stream-K slots).  Skinny M
+ * (<= 256) runs the same skinny kernels as b200_gemm_bf16, with their
+ * workspace in the array, or, where it would not fit, the cluster kernel
+ * (no workspace).  Slice counts chosen per shape always fit; only a forced
+ * one (b200_gemm_set_splits) can need more than the workspace, and such a
+ * call returns B200_ERR_TOO_LARGE.  Grids that b200_gemm_bf16 would give a
+ * stream-K tail run whole tiles here (the tail's slots exceed the array).
+ * Every call shares the array; the parts that must start at zero are
+ * cleared on the call's stream, and the flags take a new epoch per call.
+ * Calls whose executions overlap on the GPU (other streams, other threads)
  * race on it, so callers serialise them.  A pipeline wait that runs out is
- * recorded only in this array's error word, which no entry point reads.
- * The first call on a device also sets that device up (kernel attributes,
- * occupancy, the array's device address); make that first call before any
+ * recorded in the array's error word, which stays set until
+ * b200_gemm_noalloc_status reads and clears it.  The first call on a device
+ * (or of b200_gemm_noalloc_status) also sets that device up (kernel
+ * attributes, occupancy, the array's device address); make it before any
  * stream capture.  No counterpart in the reference, which has no scratch. */
 int b200_gemm_bf16_noalloc(const void* A, const void* B, void* C, int M, int N, int K, int lda,
                            int ldb, int ldc, void* stream);
+
+/* Reads (and if `clear`, resets) the error word of b200_gemm_bf16_noalloc's
+ * array on the current device: 0, or the code of the first pipeline wait
+ * that ran out in its kernels since the last clear (codes as for
+ * b200_gemm_device_status).  Synchronises the device; allocates nothing.
+ * No reference counterpart. */
+int b200_gemm_noalloc_status(int clear, int* status_out);
+
+/* The wait self-test of b200_gemm_wait_probe, recording into the
+ * allocation-free entry point's error word instead (read it with
+ * b200_gemm_noalloc_status).  Allocates nothing.  No reference counterpart. */
+int b200_gemm_noalloc_wait_probe(unsigned long long timeout_ns, void* stream);
 
 /* ---- Fused K-split over NVLink -------------------------------------------
  * One GEMM C = A B^T (M x N x K) split along K over P ranks, one process per

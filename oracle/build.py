@@ -10,7 +10,8 @@
   src/bench_core.py:36-43), plus ``ref_shim.cu`` for a C entry point.  The
   kernel files include torch headers and use TORCH_CHECK, so torch's include
   directories and libc10 are on the command line.  This step runs only where
-  the reference checkout exists (``B200_REFERENCE_DIR``); the built library is
+  the reference checkout exists (``B200_REFERENCE_DIR``, by default a
+  directory named ``reference`` beside this repository); the built library is
   what travels to the GPU machine.
 """
 from __future__ import annotations
@@ -26,7 +27,9 @@ HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "liboracle.so"
 REF_DIR = HERE / "_ref"
 REF_SO = REF_DIR / "libref_gemm.so"
-REFERENCE_DIR = Path(os.environ.get("B200_REFERENCE_DIR", "/root/reference"))
+# The reference checkout: B200_REFERENCE_DIR, else a checkout named
+# "reference" beside this repository's directory.
+REFERENCE_DIR = Path(os.environ.get("B200_REFERENCE_DIR", HERE.parent.parent / "reference"))
 REF_VERSIONS = ["v1", "v2", "v3", "v4", "v5", "v6", "v7", "v8"]
 
 

@@ -60,6 +60,23 @@ def _worker(rank, world, port, case, errq):
             rs = slice(rank * M // world, (rank + 1) * M // world)
             rows = bdist.row_shard_gemm(A[rs], Bt, gemm=lambda a, b: cpu_cast(cpu_gemm_f32(a, b)))
             assert torch.equal(rows, full[rs].to(torch.bfloat16))
+        elif case == "sampled_parity":
+            # K-split parity on sampled rows without any rank holding all of K:
+            # the right rows pass on every rank, a planted error in rank 1's
+            # block fails on every rank.
+            ks = bdist.k_slice(K, world, rank)
+            rs = slice(rank * M // world, (rank + 1) * M // world)
+            rows = full[rs].to(torch.bfloat16)
+            got = bdist.k_split_sampled_parity(rows, A[:, ks].contiguous(), Bt[:, ks].contiguous(),
+                                               per_owner=M // world)
+            assert got["pass"] and got["rows_checked"] == M, got
+            assert got["max_scaled"] < 1e-2 and got["rel_fro"] < 5e-3, got
+            bad = rows.clone()
+            if rank == 1:
+                bad[3, 5] += 4.0
+            got = bdist.k_split_sampled_parity(bad, A[:, ks].contiguous(), Bt[:, ks].contiguous(),
+                                               per_owner=M // world)
+            assert not got["pass"], got
         elif case == "rank_fails":
             if rank == 1:
                 raise SystemExit(0)          # leaves before the collective
@@ -104,6 +121,11 @@ def test_row_shard_gloo():
     assert all(v == "ok" for v in out.values()), out
 
 
+def test_k_split_sampled_parity_gloo():
+    out = run("sampled_parity")
+    assert all(v == "ok" for v in out.values()), out
+
+
 def test_failed_rank_ends_peer_collective_with_error():
     out = run("rank_fails")
     assert out[1] == "left"
@@ -123,6 +145,7 @@ def test_fused_k_split_checks_operands_and_out_before_any_call():
 
     fk = object.__new__(FusedKSplit)
     fk.world = 2
+    fk.device = torch.device("cuda", 0)
     A = torch.zeros(512, 64, dtype=torch.bfloat16)
     B = torch.zeros(256, 64, dtype=torch.bfloat16)
     with pytest.raises(ValueError):                 # CPU tensors are not on a GPU
@@ -139,3 +162,33 @@ def test_fused_k_split_checks_operands_and_out_before_any_call():
         fk._check_out(torch.empty(256, 512, dtype=torch.bfloat16)[:, ::2], 512, 256, dev)
     with pytest.raises(TypeError):
         fk._check_out(torch.empty(256, 256, dtype=torch.float32), 512, 256, dev)
+
+
+class _FakeCudaTensor:
+    """Just enough of a tensor on another GPU for FusedKSplit's checks."""
+
+    def __init__(self, shape, device):
+        self.shape, self.device, self.dtype = torch.Size(shape), torch.device(device), torch.bfloat16
+
+    def dim(self):
+        return len(self.shape)
+
+    def is_contiguous(self):
+        return True
+
+
+def test_fused_k_split_refuses_operands_on_another_gpu():
+    # The communicator lives on cuda:0; operands on cuda:1 must be refused in
+    # Python, before any pointer reaches b200_ksplit_gemm_bf16.
+    from blackwell_gemm_b200.distributed import FusedKSplit
+
+    fk = object.__new__(FusedKSplit)
+    fk.world = 2
+    fk.device = torch.device("cuda", 0)
+    fk._check_operands(_FakeCudaTensor((512, 64), "cuda:0"), _FakeCudaTensor((256, 64), "cuda:0"))
+    with pytest.raises(ValueError, match="this rank's GPU"):
+        fk._check_operands(_FakeCudaTensor((512, 64), "cuda:1"),
+                           _FakeCudaTensor((256, 64), "cuda:1"))
+    with pytest.raises(ValueError, match="one CUDA device"):
+        fk._check_operands(_FakeCudaTensor((512, 64), "cuda:0"),
+                           _FakeCudaTensor((256, 64), "cuda:1"))

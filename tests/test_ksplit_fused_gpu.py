@@ -4,10 +4,13 @@
   tile, so it must reproduce b200_gemm_bf16 bit for bit (same pair tiles, 256
   or 512 wide, same MMA order) and the oracle exactly on exact-arithmetic
   inputs.
-* Two ranks (two GPUs, one process each, NVLS off): rows must equal the
-  NCCL reduce-scatter path bit for bit (same fp32 partials; a two-term fp32
-  sum does not depend on order), match the oracle exactly on exact inputs and
-  meet the parity bar on random ones, across several calls (both receive
+* Two, four and eight ranks (one GPU and one process each, NVLS off): at two
+  ranks rows must equal the NCCL reduce-scatter path bit for bit (same fp32
+  partials, and a two-term fp32 sum does not depend on order); at more ranks
+  the kernel sums in rank order and NCCL's ring in its own order, so rows
+  must be within one bf16 ulp of NCCL's for all but a few elements.  At every
+  rank count rows must match the oracle exactly on exact inputs (exact sums
+  do not depend on order) and meet the parity bar on random ones, across several calls (both receive
   parities, both tile widths) and a change of shape inside the capacity.  Then one rank calls
   alone: its wait for the peer's pieces must run out (bound 5 x 0.2 s), set
   the device error word to 0x1007 and return.
@@ -135,7 +138,13 @@ def _worker(rank, world, port, q):
             rs = slice(rank * M // world, (rank + 1) * M // world)
             R = A[rs].float() @ Bt.float().T
             m = parity.metrics(rows, R, A[rs], Bt)
-            same = torch.equal(rows.view(torch.int16), nccl_rows.view(torch.int16))
+            if world == 2:
+                same = torch.equal(rows.view(torch.int16), nccl_rows.view(torch.int16))
+            else:
+                a16 = rows.view(torch.int16).int()
+                b16 = nccl_rows.view(torch.int16).int()
+                near = ((a16 - b16).abs() <= 1) & ((a16 < 0) == (b16 < 0))
+                same = float(near.float().mean()) > 0.999
             ok &= parity.passes(m) and same
             report.append((call, M, N, K, same, m))
         capi.set_tuning(-1, 0, 0)
@@ -174,7 +183,7 @@ def _worker(rank, world, port, q):
         q.put((rank, False, traceback.format_exc()))
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_fused_k_split_on_several_gpus(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
