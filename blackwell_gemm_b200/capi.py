@@ -31,6 +31,7 @@ DEVICE_WAIT_CODES = {
     0x1006: "wait probe",
     0x1007: "K-split: a peer's piece of an own tile never arrived",
     0x1008: "stream-K: an earlier CTA's partial tile never arrived",
+    0x1009: "dynamic dealing: a slot of the pair's unit ring",
 }
 
 KSPLIT_HANDLE_BYTES = 128
@@ -53,6 +54,7 @@ SIGNATURES = {
     "b200_gemm_set_splits": (_i, [_i]),
     "b200_gemm_set_skinny_mode": (_i, [_i]),
     "b200_gemm_set_stream_k": (_i, [_i]),
+    "b200_gemm_set_dynamic": (_i, [_i]),
     "b200_gemm_get_splits": (_i, [_i, _i, _i, _ip]),
     "b200_gemm_profile_rows": (_i, [_i, _i, _i, _ip]),
     "b200_gemm_device_status": (_i, [_i, _ip]),
@@ -171,6 +173,11 @@ def set_splits(splits: int) -> None:
 def set_stream_k(mode: int) -> None:
     """0 off, 1 when the last wave is short (default), 2 whenever it is partial."""
     check(lib().b200_gemm_set_stream_k(mode), "b200_gemm_set_stream_k")
+
+
+def set_dynamic(mode: int) -> None:
+    """1 dynamic dealing of whole tiles (default), 0 static."""
+    check(lib().b200_gemm_set_dynamic(mode), "b200_gemm_set_dynamic")
 
 
 def set_skinny_mode(mode: int) -> None:

@@ -97,6 +97,23 @@ std::atomic<int> g_group{0};
 std::atomic<int> g_splits{-1};
 std::atomic<int> g_skinny{-1};
 std::atomic<int> g_streamk{-1};
+std::atomic<int> g_dynamic{-1};
+
+// Dynamic dealing of the pair kernels' data-parallel units (1) or the
+// static deal pair p -> units p, p + P, ... (0, default).  Measured same
+// process, cold L2 (TFLOP/s static / dynamic): 8192^3 1597 / 1593, 16384^3
+// 1375 / 1375, 8192x6144x4096 1553 / 1496, 8192x4096x4096 1584 / 1542,
+// 8192x28672x4096 1547 / 1550, 8192x4096x14336 1535 / 1523, 4096^3 1502 /
+// 1465: the static deal is kept.  Initialised from B200_GEMM_DYNAMIC,
+// changeable through b200_gemm_set_dynamic.
+int dynamic_mode() {
+  int v = g_dynamic.load();
+  if (v < 0) {
+    v = env_int("B200_GEMM_DYNAMIC", 0, 0, 1);
+    g_dynamic.store(v);
+  }
+  return v;
+}
 
 // Below this wave efficiency a 256 x 256 grid gets a stream-K tail (mode 1).
 constexpr double kStreamKWaveEfficiency = 0.97;
@@ -477,6 +494,41 @@ int choose_splits(int M, int N, int k_blocks, int pairs) {
   return s < 1 ? 1 : s;
 }
 
+// Per-(device, stream) counters of the dynamic dealing (GemmArgs::sched):
+// two words, zero at every launch -- each launch's last pair sets them back
+// to zero -- so consecutive launches on one stream share them and launches
+// on different streams never do.  Created on a stream's first call
+// (cudaMalloc, cleared on the stream itself); null when none can be made.
+struct StreamSched {
+  int device;
+  cudaStream_t stream;
+  unsigned int* words;
+};
+constexpr int kMaxStreamScheds = 256;
+StreamSched g_stream_sched[kMaxStreamScheds];
+int g_num_stream_sched = 0;
+
+unsigned int* stream_sched(cudaStream_t stream) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  for (int i = 0; i < g_num_stream_sched; ++i)
+    if (g_stream_sched[i].device == dev && g_stream_sched[i].stream == stream)
+      return g_stream_sched[i].words;
+  if (g_num_stream_sched == kMaxStreamScheds) return nullptr;
+  unsigned int* p = nullptr;
+  if (cudaMalloc(&p, 256) != cudaSuccess || cudaMemsetAsync(p, 0, 256, stream) != cudaSuccess) {
+    cudaGetLastError();
+    if (p) cudaFree(p);
+    return nullptr;
+  }
+  g_stream_sched[g_num_stream_sched++] = {dev, stream, p};
+  return p;
+}
+
 template <bool kProfile, int V, int kOut, bool kSK = false>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmArgs args,
            int splits, const DeviceState& d, cudaStream_t stream) {
@@ -493,9 +545,35 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
   const long long units =
       args.sk_tiles > 0 ? d.max_pairs[V] : (long long)args.dp_tiles * args.splits;
   const int pairs = (int)(units < d.max_pairs[V] ? units : d.max_pairs[V]);
+  // Dynamic dealing pays only past the first wave.  Counters: the stream's
+  // own outside capture; under capture (a graph may be replayed on another
+  // stream) a pair of words from the pool, cleared in the graph.  A caller
+  // that set args.sched (the allocation-free entry point) keeps its own.
+  char* sched_ws = nullptr;
+  if (args.sched == nullptr && dynamic_mode() != 0 && args.dp_tiles * (long long)args.splits > pairs) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+      cudaGetLastError();
+      cap = cudaStreamCaptureStatusActive;
+    }
+    if (cap == cudaStreamCaptureStatusNone) {
+      args.sched = stream_sched(stream);
+    } else if (d.pool != nullptr) {
+      if (cudaMallocFromPoolAsync(reinterpret_cast<void**>(&sched_ws), 256, d.pool, stream) ==
+              cudaSuccess &&
+          cudaMemsetAsync(sched_ws, 0, 256, stream) == cudaSuccess) {
+        args.sched = reinterpret_cast<unsigned int*>(sched_ws);
+      } else {
+        cudaGetLastError();
+        return B200_ERR_LAUNCH;
+      }
+    }
+  }
   pair_kernel<kProfile, V, kOut, kSK><<<2 * pairs, C::kThreads, C::kSmemBytes, stream>>>(
       ta, tb, tc, args);
-  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
+  const int st = cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH;
+  if (sched_ws != nullptr) cudaFreeAsync(sched_ws, stream);
+  return st;
 }
 
 // bf16 GEMM with configuration v.  tb maps B with 128-row boxes (the
@@ -1045,6 +1123,7 @@ GemmArgs base_args(int M, int N, int K, const DeviceState& d, long long* prof, i
   args.sk_slots = nullptr;
   args.sk_flags = nullptr;
   args.sk_epoch = 0;
+  args.sched = nullptr;
   // Operand loads are marked evict-last: at 8192^3 (and the projection
   // shapes) that keeps A and B ahead of the output and of other data in L2
   // and was measured ~2% faster, at equal power, than the default policy.
@@ -1525,6 +1604,12 @@ int b200_gemm_set_stream_k(int mode) {
   return B200_OK;
 }
 
+int b200_gemm_set_dynamic(int mode) {
+  if (mode < 0 || mode > 1) return B200_ERR_INVALID_ARGUMENT;
+  g_dynamic.store(mode);
+  return B200_OK;
+}
+
 int b200_gemm_set_skinny_mode(int mode) {
   if (mode < 0 || mode > 3) return B200_ERR_INVALID_ARGUMENT;
   g_skinny.store(mode);
@@ -1728,6 +1813,8 @@ int b200_ksplit_destroy(b200_ksplit_comm* c) {
 // Layout of the scratch array (16 MiB):
 //   [0, 4)            error word of the kernels this entry point launches
 //                     (sticky: read and cleared by b200_gemm_noalloc_status)
+//   [128, 136)        counters of the pair kernels' dynamic dealing (zero
+//                     between launches: each launch's last pair resets them)
 //   [256, 64 KiB)     epoch flags of the skinny stream-K kernel (only flags
 //                     live here, so values left by earlier calls are older
 //                     epochs and nothing needs clearing between calls)
@@ -1740,6 +1827,7 @@ int b200_ksplit_destroy(b200_ksplit_comm* c) {
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 16u << 20;
+constexpr size_t kNoAllocSchedOffset = 128;
 constexpr size_t kNoAllocFlagsOffset = 256;
 constexpr size_t kNoAllocWorkspaceOffset = 64u << 10;
 constexpr size_t kNoAllocFlagCount = (kNoAllocWorkspaceOffset - kNoAllocFlagsOffset) / 4;
@@ -1865,6 +1953,9 @@ int run_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K,
       encode_2d(&tb, B, K, N, ldb, kSlabK, kCtaN) != B200_OK)
     return B200_ERR_TENSOR_MAP;
   GemmArgs args = base_args(M, N, K, nd->launch, nullptr, 0);
+  // Dynamic dealing's counters: two words of the array, zero when the
+  // library is loaded and set back to zero by every launch's last pair.
+  if (dynamic_mode() != 0) args.sched = reinterpret_cast<unsigned int*>(nd->scratch + kNoAllocSchedOffset);
   if (splits > 1) {
     // The split-K accumulator must start at zero: the array keeps the
     // previous call's contents.

@@ -80,6 +80,11 @@ struct GemmArgs {
   float* sk_slots;          // [pair][pieces][kPieceFloats]: the pair's piece of a tile it does not finish
   unsigned int* sk_flags;   // [pair][pieces], below sk_epoch at launch
   unsigned int sk_epoch;    // value a raised flag takes in this call
+  // Dynamic dealing of the data-parallel units (null: static, pair p takes
+  // units p, p + P, ...): sched[0] counts tickets taken after the first
+  // wave, sched[1] pairs that are done; both 0 at launch, and the last pair
+  // to finish sets them back to 0 (see WorkIter).
+  unsigned int* sched;
 };
 
 __device__ __forceinline__ uint64_t l2_policy(int code) {
@@ -97,6 +102,7 @@ enum : int {
   kErrWaitProbe = 0x1006,     // self-test kernel (wait that nothing releases)
   kErrWaitPeer = 0x1007,      // K-split: a peer's piece of an own tile never arrived
   kErrWaitPartial = 0x1008,   // stream-K: an earlier CTA's partial tile never arrived
+  kErrWaitSched = 0x1009,     // dynamic dealing: a slot of the pair's unit ring
 };
 
 // Intra-kernel profiler tags; numbering and row format follow the
@@ -157,6 +163,7 @@ __device__ __forceinline__ uint32_t ld_volatile_shared(uint32_t addr) {
 // CTAs' abort words and returns false so the caller can leave its loop and
 // reach the teardown.  The bound is timeout_ns plus at most one burst of
 // polls.
+template <bool kAcqCluster = false>
 __device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, const WaitCtx& w, int code,
                                        bool honour_abort) {
   const unsigned long long t0 = globaltimer_ns();
@@ -164,7 +171,8 @@ __device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, const Wait
     // Poll in bursts; the abort word and the clock are read once per burst.
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+      if (kAcqCluster ? mbar_try_wait_acq_cluster(bar, parity) : mbar_try_wait(bar, parity))
+        return true;
     if (honour_abort && ld_volatile_shared(w.abort_local) != 0) return false;
     if (globaltimer_ns() - t0 > w.timeout_ns) {
       atomicCAS(w.status, 0, code);
@@ -179,6 +187,14 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, cons
                                              int code) {
   if (mbar_try_wait(bar, parity)) return true;
   return wait_slow(bar, parity, w, code, true);
+}
+
+// wait_bounded with acquire semantics at cluster scope (data written into
+// this CTA's shared memory by the other CTA of the pair).
+__device__ __forceinline__ bool wait_bounded_acq_cluster(uint32_t bar, uint32_t parity,
+                                                         const WaitCtx& w, int code) {
+  if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+  return wait_slow<true>(bar, parity, w, code, true);
 }
 
 // In place on 32 consecutive accumulator columns of one row (fp32 bits):
@@ -396,6 +412,39 @@ __device__ __forceinline__ int sk_pairs(const GemmArgs& a, int P) {
   return sk_range_pairs(a.sk_items, P);
 }
 
+// Dynamic dealing of data-parallel units.  The first wave is static (pair p
+// takes unit p); after that the pair leader's producer thread (the fetcher)
+// takes tickets from the global counter GemmArgs::sched[0] -- unit = P +
+// ticket -- and publishes each unit it will process in a ring of
+// kSchedDepth slots held in both CTAs' shared memory (a unit, or -1 for "no
+// more work"), with a full barrier per slot in each CTA and an empty
+// barrier per slot in the leader.  Every other role of the pair (the peer's
+// producer, the MMA thread, every epilogue warp of both CTAs) takes the units
+// from the ring in the same order and frees its slot.  Units are therefore
+// handed out in increasing order as pairs become free, so the tiles in flight
+// stay a compact window of the raster however the pairs' speeds drift, and
+// no pair idles while another still has several tiles queued.  The ring
+// never deadlocks: the fetcher waits for slot reuse only on units at least
+// kSchedDepth behind, whose data it has already loaded.
+constexpr int kSchedDepth = 8;
+
+struct SchedRing {
+  uint32_t full;          // shared::cta address of this CTA's full[0]
+  uint32_t full_self;     // shared::cluster address of this CTA's full[0] (fetcher)
+  uint32_t unit;          // shared::cta address of this CTA's unit[0]
+  uint32_t empty_leader;  // shared::cluster address of the leader's empty[0]
+  uint32_t empty_local;   // shared::cta address of the leader's empty[0] (fetcher)
+  uint32_t full_peer;     // shared::cluster address of the peer's full[0] (fetcher)
+  uint32_t unit_peer;     // shared::cluster address of the peer's unit[0] (fetcher)
+};
+
+enum SchedRole : int {
+  kSchedStatic = 0,  // GemmArgs::sched is null: pair p takes units p, p + P, ...
+  kSchedFetch = 1,   // the leader's producer thread: takes tickets, publishes units
+  kSchedTake = 2,    // one thread takes published units
+  kSchedTakeWarp = 3 // a whole warp: lane 0 takes, the unit is broadcast
+};
+
 // One pair's work, in order: its stream-K segments (a tile and a K-block
 // range within it), last tile first, then its data-parallel units.  Walking
 // the stream-K range backwards makes a pair compute the head of the tile it
@@ -405,13 +454,51 @@ __device__ __forceinline__ int sk_pairs(const GemmArgs& a, int P) {
 struct WorkIter {
   int u, dp_units, npairs;
   long long lo, pos;  // stream-K range still to walk: [lo, pos)
-  __device__ __forceinline__ void init(const GemmArgs& a, int pair, int P) {
+  int role, n, ticket;
+  unsigned int* counter;
+  SchedRing ring;
+  const WaitCtx* w;
+  __device__ __forceinline__ void init(const GemmArgs& a, int pair, int P, int sched_role = kSchedStatic,
+                                       const SchedRing* r = nullptr, const WaitCtx* wc = nullptr) {
     npairs = P;
     u = pair;
     dp_units = a.dp_tiles * a.splits;
     lo = pos = 0;
     const int G = sk_pairs(a, P);
     if (a.sk_tiles > 0 && pair < G) sk_range(pair, a.sk_items, G, &lo, &pos);
+    role = a.sched != nullptr ? sched_role : kSchedStatic;
+    counter = a.sched;
+    n = 0;
+    ticket = pair;  // the first wave is dealt statically
+    if (r != nullptr) ring = *r;
+    w = wc;
+  }
+  // Fetcher: publish the next unit (or -1) in the ring, then take the next
+  // ticket (its latency hides behind the loads of the unit just published).
+  // -2 when a wait ran out.
+  __device__ __forceinline__ int publish() {
+    const uint32_t slot = n % kSchedDepth, lap = n / kSchedDepth;
+    ++n;
+    // (acquire at cluster scope: the peer's takers read their slot before
+    // arriving, and this thread then overwrites it remotely)
+    if (!wait_bounded_acq_cluster(ring.empty_local + slot * 8u, (lap & 1u) ^ 1u, *w, kErrWaitSched))
+      return -2;
+    const int unit = ticket < dp_units ? ticket : -1;
+    st_shared_u32(ring.unit + slot * 4u, (uint32_t)unit);
+    st_cluster_u32(ring.unit_peer + slot * 4u, (uint32_t)unit);
+    mbar_arrive_release_cluster(ring.full_self + slot * 8u);
+    mbar_arrive_release_cluster(ring.full_peer + slot * 8u);
+    if (unit >= 0) ticket = npairs + (int)atomicAdd(counter, 1u);
+    return unit;
+  }
+  // Taker (one thread): the next published unit, -2 when a wait ran out.
+  __device__ __forceinline__ int take() {
+    const uint32_t slot = n % kSchedDepth, lap = n / kSchedDepth;
+    ++n;
+    if (!wait_bounded_acq_cluster(ring.full + slot * 8u, lap & 1u, *w, kErrWaitSched)) return -2;
+    const int unit = ld_shared_s32(ring.unit + slot * 4u);
+    mbar_arrive_release_cluster(ring.empty_leader + slot * 8u);
+    return unit;
   }
   // Next work: tile (tm, tn), K blocks [kb0, kb1), stream-K tile index sk_t
   // (-1 for a data-parallel unit).  False when the pair's work is done.
@@ -427,13 +514,36 @@ struct WorkIter {
         return true;
       }
     }
-    if (u < dp_units) {
-      unit_coord<kOut>(u, a, tm, tn, kb0, kb1);
-      *sk_t = -1;
+    int unit;
+    if (role == kSchedStatic) {
+      if (u >= dp_units) return false;
+      unit = u;
       u += npairs;
-      return true;
+    } else if (role == kSchedFetch) {
+      unit = publish();
+    } else if (role == kSchedTake) {
+      unit = take();
+    } else {
+      int v = 0;
+      if ((threadIdx.x & 31) == 0) v = take(); else ++n;
+      unit = __shfl_sync(0xffffffffu, v, 0);
     }
-    return false;
+    if (unit < 0) return false;
+    unit_coord<kOut>(unit, a, tm, tn, kb0, kb1);
+    *sk_t = -1;
+    return true;
+  }
+  // Fetcher, once after its loop however it ended: count this pair done; the
+  // last pair resets the counters for the next launch on the stream.  The
+  // fence orders this pair's last ticket before its "done", so no ticket is
+  // taken after the reset.
+  __device__ __forceinline__ void finish() {
+    if (role != kSchedFetch) return;
+    __threadfence();
+    if (atomicAdd(counter + 1, 1u) == (unsigned int)npairs - 1u) {
+      atomicExch(counter, 0u);
+      atomicExch(counter + 1, 0u);
+    }
   }
 };
 
@@ -463,6 +573,9 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
   __shared__ alignas(8) uint64_t bar_acc_full[kAccBufs];
   __shared__ alignas(8) uint64_t bar_acc_empty[kAccBufs];
   __shared__ alignas(8) uint64_t bar_drain;
+  __shared__ alignas(8) uint64_t bar_sched_full[kSchedDepth];
+  __shared__ alignas(8) uint64_t bar_sched_empty[kSchedDepth];
+  __shared__ int sched_unit[kSchedDepth];
   __shared__ uint32_t tmem_slot;
   __shared__ uint32_t abort_word;
 
@@ -495,6 +608,11 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       mbar_init(smem_u32(&bar_acc_empty[b]), 2 * P::kEpiWarps);  // every epilogue warp of the pair
     }
     mbar_init(smem_u32(&bar_drain), 1);
+    for (int s = 0; s < kSchedDepth; ++s) {
+      mbar_init(smem_u32(&bar_sched_full[s]), 1);  // the fetcher's publication
+      // (leader) the peer's producer, the MMA thread, every epilogue warp of the pair
+      mbar_init(smem_u32(&bar_sched_empty[s]), 2 + 2 * P::kEpiWarps);
+    }
     abort_word = 0;
     fence_mbar_init_cluster();
     prefetch_tmap(&tmap_a);
@@ -516,6 +634,15 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
   wctx.abort_local = smem_u32(&abort_word);
   wctx.abort_peer = cluster_map(smem_u32(&abort_word), rank ^ 1u);
 
+  SchedRing ring;
+  ring.full = smem_u32(&bar_sched_full[0]);
+  ring.full_self = cluster_map(ring.full, rank);
+  ring.unit = smem_u32(&sched_unit[0]);
+  ring.empty_leader = cluster_map(smem_u32(&bar_sched_empty[0]), 0);
+  ring.empty_local = smem_u32(&bar_sched_empty[0]);
+  ring.full_peer = cluster_map(ring.full, rank ^ 1u);
+  ring.unit_peer = cluster_map(ring.unit, rank ^ 1u);
+
   if constexpr (kProfile) {
     if (lane == 0) prof.stop();
   }
@@ -530,7 +657,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       uint32_t filled = 0;  // ring slots this producer has filled so far
       bool ok = true;
       WorkIter wi;
-      wi.init(args, pair, npairs);
+      wi.init(args, pair, npairs, rank == 0 ? kSchedFetch : kSchedTake, &ring, &wctx);
       int tm, tn, kb0, kb1, skt;
       while (ok && wi.template next<kOut, kSK>(args, &tm, &tn, &kb0, &kb1, &skt)) {
         const int a_row = tm * kPairM + (int)rank * kCtaM;
@@ -563,6 +690,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
       }
+      wi.finish();
       if constexpr (kProfile) prof.flush();
     }
     __syncwarp();
@@ -577,7 +705,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
       int it = 0;
       bool ok = true;
       WorkIter wi;
-      wi.init(args, pair, npairs);
+      wi.init(args, pair, npairs, kSchedTake, &ring, &wctx);
       int tm, tn, kb0, kb1, skt;
       while (ok && wi.template next<kOut, kSK>(args, &tm, &tn, &kb0, &kb1, &skt)) {
         const int my_it = it++;
@@ -641,7 +769,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     uint32_t nstore = 0;
     int it = 0;
     WorkIter wi;
-    wi.init(args, pair, npairs);
+    wi.init(args, pair, npairs, kSchedTakeWarp, &ring, &wctx);
     int tm, tn, kb0, kb1, skt;
     while (wi.template next<kOut, kSK>(args, &tm, &tn, &kb0, &kb1, &skt)) {
       const int my_it = it++;

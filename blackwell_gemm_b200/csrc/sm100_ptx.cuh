@@ -92,6 +92,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+// The same poll with acquire semantics at cluster scope: a thread of the
+// other CTA wrote shared memory of this CTA (st.shared::cluster) and then
+// arrived with mbar_arrive_release_cluster; after this wait succeeds those
+// writes are visible.
+__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done) : "r"(bar), "r"(parity), "n"(kPollSuspendNs) : "memory");
+  return done != 0;
+}
+
+// Arrive on a barrier (shared::cluster address, local or peer) with release
+// semantics at cluster scope: this thread's earlier shared-memory accesses,
+// in either CTA, happen before the phase completes for a waiter that
+// acquires at cluster scope.
+__device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];"
+               :: "r"(bar) : "memory");
+}
+
+__device__ __forceinline__ int ld_shared_s32(uint32_t addr) {
+  int v;
+  asm volatile("ld.shared.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 // Arrive on a barrier given by its shared::cluster address (local or peer).
 // Release semantics at CTA scope: the data these arrivals publish is either
 // written by the async proxy (TMA, tracked by the transaction count) or is

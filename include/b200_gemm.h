@@ -114,6 +114,18 @@ int b200_gemm_set_skinny_mode(int mode);
  * tiles with cluster launch control). */
 int b200_gemm_set_stream_k(int mode);
 
+/* Dealing of whole tiles to the persistent pairs: 0 = static (default;
+ * B200_GEMM_DYNAMIC overrides): pair p takes tiles p, p + P, ...; 1 =
+ * dynamic: after a static first wave, each pair takes its next tile from a
+ * device counter the moment it needs one, so the tiles in flight stay a
+ * compact window of the raster and no pair idles while another has tiles
+ * queued (measured no faster on the configuration shapes, slower on some:
+ * the static deal stays the default).  The counters are two words per (device,
+ * stream), made on the stream's first call (cudaMalloc) and left at zero by
+ * every launch.  No reference counterpart (the reference steals work with
+ * cluster launch control, src/kernels/kernel_v8.cu:608-653). */
+int b200_gemm_set_dynamic(int mode);
+
 /* Same GEMM with the intra-kernel profiler on (never split).  `profiler` is a device int64
  * buffer of rows x (1 + 4 * num_entries) entries, rows from
  * b200_gemm_profile_rows; row r = block * warps_per_cta + warp (warps per
