@@ -53,6 +53,7 @@ SIGNATURES = {
                                      ctypes.c_float, _vp, _i, _vp]),
     "b200_gemm_set_splits": (_i, [_i]),
     "b200_gemm_set_skinny_mode": (_i, [_i]),
+    "b200_gemm_set_skinny_tiles": (_i, [_i]),
     "b200_gemm_set_stream_k": (_i, [_i]),
     "b200_gemm_set_dynamic": (_i, [_i]),
     "b200_gemm_get_splits": (_i, [_i, _i, _i, _ip]),
@@ -173,6 +174,11 @@ def set_splits(splits: int) -> None:
 def set_stream_k(mode: int) -> None:
     """0 off, 1 when the last wave is short (default), 2 whenever it is partial."""
     check(lib().b200_gemm_set_stream_k(mode), "b200_gemm_set_stream_k")
+
+
+def set_skinny_tiles(tiles: int) -> None:
+    """Blocks of B per skinny stream-K tile: 1, 2, or 0 (chosen)."""
+    check(lib().b200_gemm_set_skinny_tiles(tiles), "b200_gemm_set_skinny_tiles")
 
 
 def set_dynamic(mode: int) -> None:

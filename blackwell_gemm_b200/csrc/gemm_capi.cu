@@ -138,6 +138,28 @@ int skinny_l2_hint() {
   return h;
 }
 
+std::atomic<int> g_skinny_tiles{-1};
+
+// 128-row blocks of B per tile of the skinny stream-K kernel (blocks of a
+// tile share each A slab, so A's share of every SM's L2 inflow falls
+// with their number): 1, 2 (M <= 128 only), or 0 = chosen: one.  Two were
+// measured slower at every shape (cold-L2 medians, us, one / two blocks):
+// N = K = 8192: M = 16 36.2 / 38.1, 64 38.1 / 40.2, 128 42.3 / 46.4;
+// N = K = 4096: M = 128 25.9 / 32.0; N = 28672, K = 4096: M = 128 58.6 /
+// 68.9 -- each CTA range then cuts twice as many rows of B into partial
+// tiles, so the in-kernel fix-up moves twice the slot bytes at the end.
+// Initialised from B200_GEMM_SKINNY_TILES, changeable through
+// b200_gemm_set_skinny_tiles.
+int skinny_stream_tiles(int M) {
+  int v = g_skinny_tiles.load();
+  if (v < 0) {
+    v = env_int("B200_GEMM_SKINNY_TILES", 0, 0, 2);
+    g_skinny_tiles.store(v);
+  }
+  if (M > 128) return 1;
+  return v == 0 ? 1 : v;
+}
+
 // Skinny-M path (M <= 256): 0 = off, 1 = chosen per shape, 2 = the cluster
 // kernel for every M, 3 = the stream-K kernel for every M.  Initialised from
 // B200_GEMM_SKINNY, changeable through b200_gemm_set_skinny_mode.
@@ -246,17 +268,27 @@ int init_variants(int sms, int* max_pairs) {
 constexpr int skinny_tiles(int mp) { return mp > 0 ? 2 : 1; }
 
 // kSlabs: K slabs per stage asked for; each kernel gets the most that fit.
+// Largest stream-K tile (128-row blocks of B sharing each A slab) whose
+// double-buffered accumulator fits in TMEM: two blocks up to Mp = 128.
+constexpr int skinny_stream_max_tiles(int mp) { return 2 * 2 * mp <= 512 ? 2 : 1; }
+
+template <int kMp, int kSlabs, int kTiles>
+bool set_skinny_stream_limit() {
+  constexpr int kSs = skinny_fit_slabs(kMp, kSlabs, kTiles);
+  return cudaFuncSetAttribute(gemm_skinny_stream_kernel<kMp, kSs, kTiles>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              SkinnyCfg<kMp, kSs, kTiles>::kSmemBytes) == cudaSuccess;
+}
+
 template <int kMp, int kSlabs>
 bool set_skinny_limit() {
   constexpr int kT = skinny_tiles(kMp);
   constexpr int kSp = skinny_fit_slabs(kMp, kSlabs, kT);
-  constexpr int kSs = skinny_fit_slabs(kMp, kSlabs);
   return cudaFuncSetAttribute(gemm_skinny_kernel<kMp, kSp, kT>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                               SkinnyCfg<kMp, kSp, kT>::kSmemBytes) == cudaSuccess &&
-         cudaFuncSetAttribute(gemm_skinny_stream_kernel<kMp, kSs>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              SkinnyCfg<kMp, kSs>::kSmemBytes) == cudaSuccess;
+         set_skinny_stream_limit<kMp, kSlabs, 1>() &&
+         set_skinny_stream_limit<kMp, kSlabs, skinny_stream_max_tiles(kMp)>();
 }
 
 template <int kSlabs>
@@ -818,11 +850,11 @@ long long stream_owner_host(long long x, long long total, int G) {
   return ((x + 1) * G + total - 1) / total - 1;
 }
 
-template <int kMp, int kSlabs>
+template <int kMp, int kSlabs, int kTiles>
 int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, int K, int lda,
                          int ldb, int ldc, DeviceState& d, cudaStream_t stream,
                          const Scratch* scratch) {
-  using P = SkinnyCfg<kMp, kSlabs>;
+  using P = SkinnyCfg<kMp, kSlabs, kTiles>;
   CUtensorMap tb, ta, tc;
   if (encode_2d(&tb, B, K, N, ldb, kSlabK, P::kRowsB) != B200_OK ||
       encode_2d(&ta, A, K, M, lda, kSlabK, kMp) != B200_OK ||
@@ -833,7 +865,7 @@ int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, in
   args.M = M;
   args.N = N;
   args.K = K;
-  args.tiles = (int)ceil_div(N, P::kRowsB);
+  args.tiles = (int)ceil_div(N, kTiles * P::kRowsB);
   args.k_blocks = (int)ceil_div(K, P::kBK);
   args.total = (long long)args.tiles * args.k_blocks;
   const int G = (int)(args.total < d.sms ? args.total : d.sms);
@@ -849,7 +881,8 @@ int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, in
   args.timeout_ns = g_timeout_ns.load();
   const size_t nflags = (size_t)args.tiles * max_seg * 4;
   const size_t flag_bytes = (size_t)ceil_div((long long)nflags * 4, 256) * 256;
-  const size_t slot_bytes = (size_t)args.tiles * max_seg * kMp * P::kRowsB * sizeof(float);
+  const size_t slot_bytes =
+      (size_t)args.tiles * max_seg * kTiles * kMp * P::kRowsB * sizeof(float);
   char* ws = nullptr;
   int st = B200_OK;
   if (scratch != nullptr) {
@@ -903,8 +936,8 @@ int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, in
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, gemm_skinny_stream_kernel<kMp, kSlabs>, tb, ta, tc, args) !=
-        cudaSuccess) {
+    if (cudaLaunchKernelEx(&cfg, gemm_skinny_stream_kernel<kMp, kSlabs, kTiles>, tb, ta, tc,
+                           args) != cudaSuccess) {
       cudaGetLastError();
       st = B200_ERR_LAUNCH;
     }
@@ -917,14 +950,15 @@ template <int kSlabs>
 int run_skinny_stream_slabs(const void* A, const void* B, void* C, int M, int N, int K, int lda,
                             int ldb, int ldc, DeviceState& d, cudaStream_t stream,
                             const Scratch* scratch) {
-#define B200_SKS(MP)                                                                         \
-  launch_skinny_stream<MP, skinny_fit_slabs(MP, kSlabs)>(A, B, C, M, N, K, lda, ldb, ldc, d, \
-                                                         stream, scratch)
-  if (M <= 16) return B200_SKS(16);
-  if (M <= 32) return B200_SKS(32);
-  if (M <= 64) return B200_SKS(64);
-  if (M <= 128) return B200_SKS(128);
-  return B200_SKS(256);
+#define B200_SKS(MP, T)                                                                    \
+  launch_skinny_stream<MP, skinny_fit_slabs(MP, kSlabs, T), T>(A, B, C, M, N, K, lda, ldb, ldc, \
+                                                               d, stream, scratch)
+  const bool two = skinny_stream_tiles(M) == 2;
+  if (M <= 16) return two ? B200_SKS(16, 2) : B200_SKS(16, 1);
+  if (M <= 32) return two ? B200_SKS(32, 2) : B200_SKS(32, 1);
+  if (M <= 64) return two ? B200_SKS(64, 2) : B200_SKS(64, 1);
+  if (M <= 128) return two ? B200_SKS(128, 2) : B200_SKS(128, 1);
+  return B200_SKS(256, 1);
 #undef B200_SKS
 }
 
@@ -1083,12 +1117,14 @@ int skinny_slices(int M, int N, int K, const DeviceState* d) {
   }
   const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
   if (mode == 3 || (mode == 1 && skinny_use_stream(M, N, K))) {
-    // stream-K: the most CTAs any one block of B is cut between
-    const long long kb = ceil_div(K, skinny_fit_slabs(mp, skinny_slabs()) * kSlabK);
-    const long long total = tiles * kb;
+    // stream-K: the most CTAs any one tile of B is cut between
+    const int st = skinny_stream_tiles(M);
+    const long long kb = ceil_div(K, skinny_fit_slabs(mp, skinny_slabs(), st) * kSlabK);
+    const long long stiles = ceil_div(N, 128LL * st);
+    const long long total = stiles * kb;
     const int G = (int)(total < (d ? d->sms : 148) ? total : (d ? d->sms : 148));
     long long most = 1;
-    for (long long t = 0; t < tiles; ++t) {
+    for (long long t = 0; t < stiles; ++t) {
       const long long c = stream_owner_host(t * kb + kb - 1, total, G) -
                           stream_owner_host(t * kb, total, G) + 1;
       if (c > most) most = c;
@@ -1607,6 +1643,12 @@ int b200_gemm_set_stream_k(int mode) {
 int b200_gemm_set_dynamic(int mode) {
   if (mode < 0 || mode > 1) return B200_ERR_INVALID_ARGUMENT;
   g_dynamic.store(mode);
+  return B200_OK;
+}
+
+int b200_gemm_set_skinny_tiles(int tiles) {
+  if (tiles < 0 || tiles > 2) return B200_ERR_INVALID_ARGUMENT;
+  g_skinny_tiles.store(tiles);
   return B200_OK;
 }
 

@@ -1014,7 +1014,9 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
         if (lane == 0) prof.stop();
       }
     }
-    if (lane == 0) bulk_wait_group<0>();
+    // Only the staging buffers' reads must finish before the CTA's shared
+    // memory goes away; the stores' global writes complete with the grid.
+    if (lane == 0) bulk_wait_group_read<0>();
     if constexpr (kProfile) {
       if (lane == 0) prof.flush();
     }

@@ -516,11 +516,11 @@ namespace b200 {
 struct SkinnyStreamArgs {
   int M, N, K;
   int l2_hint;
-  int tiles;         // ceil(N / 128)
+  int tiles;         // ceil(N / (kTiles x 128))
   int k_blocks;      // K blocks per tile, ceil(K / kBK)
   long long total;   // tiles x k_blocks
   int max_seg;       // slots per tile
-  float* slots;      // [tiles][max_seg][4 quarters][kMp][32] fp32
+  float* slots;      // [tiles][max_seg][4 quarters][kTiles x kMp][32] fp32
   unsigned int* flags;  // [tiles][max_seg][4], below `epoch` at launch
   unsigned int epoch;   // value a raised flag takes in this call
   int* status;
@@ -532,15 +532,22 @@ __device__ __forceinline__ int stream_owner(long long x, long long total, int G)
   return (int)(((x + 1) * G + total - 1) / total) - 1;
 }
 
-template <int kMp, int kSlabs>
+template <int kMp, int kSlabs, int kTiles = 1>
 __global__ void __launch_bounds__(192, 1)
 gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 64 x 128
                           const __grid_constant__ CUtensorMap tmap_a,   // M x K, box 64 x Mp
                           const __grid_constant__ CUtensorMap tmap_c,   // C bf16 M x N, box 32 x kChunk
                           const SkinnyStreamArgs args) {
-  using P = SkinnyCfg<kMp, kSlabs>;
+  using P = SkinnyCfg<kMp, kSlabs, kTiles>;
+  static_assert(P::kAccBufs == 2, "the stream-K kernel double-buffers its accumulator");
   constexpr int kStages = P::kStages;
   constexpr int kChunk = P::kChunk;
+  // A tile is kTiles 128-row blocks of B sharing each A slab; its
+  // accumulator is kMpT = kTiles x Mp TMEM columns (block i at i x Mp), read
+  // by the epilogue in kMpT / kChunk chunks, kCpb of them per block.
+  constexpr int kMpT = kTiles * kMp;
+  constexpr int kTileRows = kTiles * P::kRowsB;
+  constexpr int kCpb = kMp / kChunk;
   extern __shared__ uint8_t smem_raw[];
   __shared__ alignas(8) uint64_t bar_full[kStages];
   __shared__ alignas(8) uint64_t bar_empty[kStages];
@@ -617,9 +624,11 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
           const uint32_t fb = smem_u32(&bar_full[stage]);
           mbar_arrive_expect_tx(fb, P::kStageBytes);
 #pragma unroll
-          for (int sl = 0; sl < kSlabs; ++sl)
-            tma_load_2d_hint(sb + sl * P::kSlabB, &tmap_b, kb * P::kBK + sl * kSlabK,
-                             t * P::kRowsB, fb, pol_b);
+          for (int i = 0; i < kTiles; ++i)
+#pragma unroll
+            for (int sl = 0; sl < kSlabs; ++sl)
+              tma_load_2d_hint(sb + (i * kSlabs + sl) * P::kSlabB, &tmap_b,
+                               kb * P::kBK + sl * kSlabK, t * kTileRows + i * P::kRowsB, fb, pol_b);
 #pragma unroll
           for (int sl = 0; sl < kSlabs; ++sl)
             tma_load_2d_hint(sb + P::kBytesB + sl * P::kSlabA, &tmap_a, kb * P::kBK + sl * kSlabK,
@@ -641,7 +650,7 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
         if (!wait_bounded(smem_u32(&bar_acc_empty[buf]), acc_phase ^ 1u, wctx, kErrWaitAccEmpty))
           break;
         tc_fence_after_sync();
-        const uint32_t d_tmem = tmem_base + buf * kMp;
+        const uint32_t d_tmem = tmem_base + buf * kMpT;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bounded(smem_u32(&bar_full[stage]), phase, wctx, kErrWaitFull)) {
             ok = false;
@@ -651,12 +660,15 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
           const uint32_t sb = smem_base + stage * P::kStageBytes;
 #pragma unroll
           for (int sl = 0; sl < kSlabs; ++sl) {
-            const uint64_t bdesc = make_sdesc_k128(sb + sl * P::kSlabB);
             const uint64_t adesc = make_sdesc_k128(sb + P::kBytesB + sl * P::kSlabA);
 #pragma unroll
             for (int k = 0; k < kSlabK / kMmaK; ++k)
-              umma_bf16_1(d_tmem, bdesc + 2ull * k, adesc + 2ull * k, idesc,
-                          (kb != kb0 || sl != 0 || k != 0) ? 1u : 0u);
+#pragma unroll
+              for (int i = 0; i < kTiles; ++i) {
+                const uint64_t bdesc = make_sdesc_k128(sb + (i * kSlabs + sl) * P::kSlabB);
+                umma_bf16_1(d_tmem + i * kMp, bdesc + 2ull * k, adesc + 2ull * k, idesc,
+                            (kb != kb0 || sl != 0 || k != 0) ? 1u : 0u);
+              }
           }
           umma_commit_1(smem_u32(&bar_empty[stage]));
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
@@ -686,6 +698,7 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
     // through this warp's staging buffers ([kChunk m][32 n] bf16) at lane
     // quarter q of tile t.
     auto store_bf16 = [&](const uint32_t* v, int t, int q, int c) {
+      // chunk c: block c / kCpb of the tile, rows (c % kCpb) kChunk .. of C
       const uint32_t sb = my_store + (nstore & 1u) * P::kStoreBuf;
       if (lane == 0) bulk_wait_group_read<1>();
       __syncwarp();
@@ -697,7 +710,8 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_store_2d(&tmap_c, sb, t * P::kRowsB + q * 32, c * kChunk);
+        tma_store_2d(&tmap_c, sb, t * kTileRows + (c / kCpb) * P::kRowsB + q * 32,
+                     (c % kCpb) * kChunk);
         bulk_commit_group();
       }
       ++nstore;
@@ -712,21 +726,21 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
         break;
       }
       tc_fence_after_sync();
-      const uint32_t tbase = tmem_base + buf * kMp + ((uint32_t)(quarter * 32) << 16);
+      const uint32_t tbase = tmem_base + buf * kMpT + ((uint32_t)(quarter * 32) << 16);
       const bool whole = kb0 == 0 && kb1 == KB;
       const int first = stream_owner((long long)t * KB, args.total, G);
       const int j = (int)blockIdx.x - first;
-      float* slot = args.slots + ((long long)t * args.max_seg + j) * kMp * P::kRowsB +
-                    quarter * kMp * 32 + lane;
+      float* slot = args.slots + ((long long)t * args.max_seg + j) * kMpT * P::kRowsB +
+                    quarter * kMpT * 32 + lane;
 #pragma unroll 1
-      for (int c = 0; c < kMp / kChunk; ++c) {
+      for (int c = 0; c < kMpT / kChunk; ++c) {
         uint32_t v[kChunk];
         if constexpr (kChunk == 16)
           tmem_ld_32x32b_x16(tbase + c * 16, *reinterpret_cast<uint32_t(*)[16]>(v));
         else
           tmem_ld_32x32b_x32(tbase + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v));
         tmem_wait_ld();
-        if (c == kMp / kChunk - 1) {
+        if (c == kMpT / kChunk - 1) {
           tc_fence_before_sync();
           __syncwarp();
           if (lane == 0) mbar_arrive_local(smem_u32(&bar_acc_empty[buf]));
@@ -769,7 +783,7 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
     // stores it.  (Bulk copies of the granules
     // need a generic-to-async proxy fence first, which waits for this
     // warp's C stores still in flight and cost more than the loads.)
-    constexpr int kChunks = kMp / kChunk;
+    constexpr int kChunks = kMpT / kChunk;
     constexpr int kPieces = 4 * kChunks;
     // At most a whole tile (n = 2) plus a third of another (n >= 3).
     constexpr int kMaxMine = (kPieces + kPieces / 3) / 4 + 2;
@@ -834,11 +848,11 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
     // rounded and stored when its last granule has been added.
     constexpr int kVec = kChunk / 4;
     constexpr int kRound = 4;
-    const long long slot_floats = (long long)kMp * P::kRowsB;
+    const long long slot_floats = (long long)kMpT * P::kRowsB;
     auto granule = [&](int x, int sl) {
       const int f = mine[x] >> 8, pc = mine[x] & 255;
       return args.slots + ((long long)fix_t[f] * args.max_seg + sl) * slot_floats +
-             ((pc & 3) * kMp + (pc >> 2) * kChunk) * 32 + 4 * lane;
+             ((pc & 3) * kMpT + (pc >> 2) * kChunk) * 32 + 4 * lane;
     };
     auto store_piece = [&](const float4* acc, int x) {
       const int f = mine[x] >> 8, pc = mine[x] & 255;
@@ -855,7 +869,9 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_store_2d(&tmap_c, sb, fix_t[f] * P::kRowsB + (pc & 3) * 32, (pc >> 2) * kChunk);
+        tma_store_2d(&tmap_c, sb,
+                     fix_t[f] * kTileRows + ((pc >> 2) / kCpb) * P::kRowsB + (pc & 3) * 32,
+                     ((pc >> 2) % kCpb) * kChunk);
         bulk_commit_group();
       }
       ++nstore;
@@ -902,7 +918,8 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
         }
       }
     }
-    if (lane == 0) bulk_wait_group<0>();
+    // (the staging buffers' reads only: the stores' global writes complete with the grid)
+    if (lane == 0) bulk_wait_group_read<0>();
     __syncwarp();
   }
 #undef B200_FOR_SEGMENTS

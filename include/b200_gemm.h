@@ -100,6 +100,13 @@ int b200_gemm_get_splits(int M, int N, int K, int* splits);
  * the mode.  No reference counterpart. */
 int b200_gemm_set_skinny_mode(int mode);
 
+/* 128-row blocks of B per tile of the skinny stream-K kernel: 1, 2 (a
+ * tile's two blocks share each slab of A, halving A's share of every SM's
+ * L2 inflow; M <= 128 only; measured slower: twice the in-kernel fix-up) or
+ * 0 = chosen, one (default; B200_GEMM_SKINNY_TILES overrides).  No
+ * reference counterpart. */
+int b200_gemm_set_skinny_tiles(int tiles);
+
 /* Stream-K tail of the 256 x 256 pair-tile kernels: when the tiles are more than
  * one wave of the persistent grid but not a whole number of waves, the whole
  * waves run as usual and the remaining tiles' (tile, K block) items are split

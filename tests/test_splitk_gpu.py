@@ -271,3 +271,24 @@ def test_skinny_stream_k_graph_replays_and_streams(M):
     torch.cuda.synchronize()
     for out in outs:
         assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("tiles", [1, 2])
+@pytest.mark.parametrize("M,N,K", [(1, 1032, 520), (17, 8200, 1000), (64, 1024, 8192),
+                                   (100, 4096, 2048), (128, 24576, 1024), (128, 8192, 8192),
+                                   (128, 1160, 4096)])
+def test_skinny_stream_k_tiles_exact_bits(M, N, K, tiles):
+    """The stream-K skinny kernel with tiles of one or two 128-row blocks of
+    B (two blocks share each A slab): exact results whatever the split of a
+    tile between CTAs, including a last tile whose second block lies partly
+    or wholly past N."""
+    capi.set_skinny_mode(3)
+    capi.set_skinny_tiles(tiles)
+    try:
+        A, Bt = oracle.exact_inputs(M, N, K, seed=M + N + tiles)
+        C = bf16_gemm(dev(A), dev(Bt))
+        assert np.array_equal(bits(C), oracle.gemm_bf16(A, Bt))
+        assert capi.device_status(True) == 0
+    finally:
+        capi.set_skinny_mode(1)
+        capi.set_skinny_tiles(0)
