@@ -166,7 +166,7 @@ int skinny_stream_tiles(int M) {
 int skinny_mode() {
   int v = g_skinny.load();
   if (v < 0) {
-    v = env_int("B200_GEMM_SKINNY", 1, 0, 3);
+    v = env_int("B200_GEMM_SKINNY", 1, 0, 4);
     g_skinny.store(v);
   }
   return v;
@@ -272,12 +272,12 @@ constexpr int skinny_tiles(int mp) { return mp > 0 ? 2 : 1; }
 // double-buffered accumulator fits in TMEM: two blocks up to Mp = 128.
 constexpr int skinny_stream_max_tiles(int mp) { return 2 * 2 * mp <= 512 ? 2 : 1; }
 
-template <int kMp, int kSlabs, int kTiles>
+template <int kMp, int kSlabs, int kTiles, bool kPair = false>
 bool set_skinny_stream_limit() {
   constexpr int kSs = skinny_fit_slabs(kMp, kSlabs, kTiles);
-  return cudaFuncSetAttribute(gemm_skinny_stream_kernel<kMp, kSs, kTiles>,
+  return cudaFuncSetAttribute(gemm_skinny_stream_kernel<kMp, kSs, kTiles, kPair>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              SkinnyCfg<kMp, kSs, kTiles>::kSmemBytes) == cudaSuccess;
+                              SkinnyCfg<kMp, kSs, kTiles, kPair>::kSmemBytes) == cudaSuccess;
 }
 
 template <int kMp, int kSlabs>
@@ -288,7 +288,8 @@ bool set_skinny_limit() {
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                               SkinnyCfg<kMp, kSp, kT>::kSmemBytes) == cudaSuccess &&
          set_skinny_stream_limit<kMp, kSlabs, 1>() &&
-         set_skinny_stream_limit<kMp, kSlabs, skinny_stream_max_tiles(kMp)>();
+         set_skinny_stream_limit<kMp, kSlabs, skinny_stream_max_tiles(kMp)>() &&
+         (kMp < 32 || set_skinny_stream_limit<(kMp < 32 ? 32 : kMp), kSlabs, 1, true>());
 }
 
 template <int kSlabs>
@@ -794,6 +795,18 @@ bool skinny_use_stream(int M, int N, int K) {
   return tuning_splits() == 0 && !skinny_use_cluster(M, N, K) && M <= 128;
 }
 
+// Above M = 128, the stream-K kernel on 2-CTA pairs where the split-K
+// kernel's fp32 workspace (cleared, reduce-added into, rounded: three passes
+// and two more launches) reaches 16 MB.  Measured (cold-L2 medians, us,
+// split-K / pair stream-K / cuBLAS): M = 256, N = 28672, K = 4096: 80.2 / 69.5
+// / 66.7; N = K = 8192: 51.5 / 52.4 / 43.1; N = 4096, K = 14336: 47.4 / 48.5 /
+// 41.4.  At M <= 128 the pair kernel was ~2 us slower than the one-CTA
+// stream-K kernel at every shape (the pair TMEM allocation's launch cost).
+bool skinny_use_pair_stream(int M, int N, int K) {
+  return tuning_splits() == 0 && M > 128 && (long long)M * N >= (4LL << 20) &&
+         !skinny_use_cluster(M, N, K);
+}
+
 template <int kMp, int kSlabsWanted>
 int launch_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
                   int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi,
@@ -850,14 +863,16 @@ long long stream_owner_host(long long x, long long total, int G) {
   return ((x + 1) * G + total - 1) / total - 1;
 }
 
-template <int kMp, int kSlabs, int kTiles>
+template <int kMp, int kSlabs, int kTiles, bool kPair = false>
 int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, int K, int lda,
                          int ldb, int ldc, DeviceState& d, cudaStream_t stream,
                          const Scratch* scratch) {
-  using P = SkinnyCfg<kMp, kSlabs, kTiles>;
+  using P = SkinnyCfg<kMp, kSlabs, kTiles, kPair>;
+  // flag / slot units per tile: one, or a pair tile's two CTA halves
+  constexpr int kUnits = kPair ? 2 : 1;
   CUtensorMap tb, ta, tc;
   if (encode_2d(&tb, B, K, N, ldb, kSlabK, P::kRowsB) != B200_OK ||
-      encode_2d(&ta, A, K, M, lda, kSlabK, kMp) != B200_OK ||
+      encode_2d(&ta, A, K, M, lda, kSlabK, P::kRowsA) != B200_OK ||
       encode_2d(&tc, C, N, M, ldc, 32, P::kChunk, false, false) != B200_OK)
     return B200_ERR_TENSOR_MAP;
   SkinnyStreamArgs args;
@@ -865,10 +880,11 @@ int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, in
   args.M = M;
   args.N = N;
   args.K = K;
-  args.tiles = (int)ceil_div(N, kTiles * P::kRowsB);
+  args.tiles = (int)ceil_div(N, (kPair ? 2 : kTiles) * P::kRowsB);
   args.k_blocks = (int)ceil_div(K, P::kBK);
   args.total = (long long)args.tiles * args.k_blocks;
-  const int G = (int)(args.total < d.sms ? args.total : d.sms);
+  const int workers = kPair ? d.sms / 2 : d.sms;  // pairs or CTAs, one per SM (pair)
+  const int G = (int)(args.total < workers ? args.total : workers);
   int max_seg = 1;
   for (int t = 0; t < args.tiles; ++t) {
     const long long x0 = (long long)t * args.k_blocks;
@@ -879,10 +895,10 @@ int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, in
   args.max_seg = max_seg;
   args.status = d.status;
   args.timeout_ns = g_timeout_ns.load();
-  const size_t nflags = (size_t)args.tiles * max_seg * 4;
+  const size_t nflags = (size_t)kUnits * args.tiles * max_seg * 4;
   const size_t flag_bytes = (size_t)ceil_div((long long)nflags * 4, 256) * 256;
   const size_t slot_bytes =
-      (size_t)args.tiles * max_seg * kTiles * kMp * P::kRowsB * sizeof(float);
+      (size_t)kUnits * args.tiles * max_seg * kTiles * kMp * P::kRowsB * sizeof(float);
   char* ws = nullptr;
   int st = B200_OK;
   if (scratch != nullptr) {
@@ -924,20 +940,24 @@ int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, in
     }
   }
   if (st == B200_OK) {
-    // Cooperative: the fix-up waits on CTAs of higher index, so all G CTAs
-    // (one per SM) must be resident together.
+    // Cooperative: the fix-up waits on CTAs of higher index, so all of the
+    // grid (one CTA per SM) must be resident together.  Pairs: 2-CTA clusters.
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)G, 1, 1);
+    cfg.gridDim = dim3((unsigned)(kUnits * G), 1, 1);
     cfg.blockDim = dim3(P::kThreads, 1, 1);
     cfg.dynamicSmemBytes = P::kSmemBytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = kUnits;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, gemm_skinny_stream_kernel<kMp, kSlabs, kTiles>, tb, ta, tc,
-                           args) != cudaSuccess) {
+    cfg.numAttrs = kPair ? 2 : 1;
+    if (cudaLaunchKernelEx(&cfg, gemm_skinny_stream_kernel<kMp, kSlabs, kTiles, kPair>, tb, ta,
+                           tc, args) != cudaSuccess) {
       cudaGetLastError();
       st = B200_ERR_LAUNCH;
     }
@@ -949,10 +969,20 @@ int launch_skinny_stream(const void* A, const void* B, void* C, int M, int N, in
 template <int kSlabs>
 int run_skinny_stream_slabs(const void* A, const void* B, void* C, int M, int N, int K, int lda,
                             int ldb, int ldc, DeviceState& d, cudaStream_t stream,
-                            const Scratch* scratch) {
+                            const Scratch* scratch, bool pair = false) {
 #define B200_SKS(MP, T)                                                                    \
   launch_skinny_stream<MP, skinny_fit_slabs(MP, kSlabs, T), T>(A, B, C, M, N, K, lda, ldb, ldc, \
                                                                d, stream, scratch)
+  if (pair) {
+#define B200_SKP(MP)                                                                         \
+  launch_skinny_stream<MP, skinny_fit_slabs(MP, kSlabs), 1, true>(A, B, C, M, N, K, lda, ldb, \
+                                                                  ldc, d, stream, scratch)
+    if (M <= 32) return B200_SKP(32);
+    if (M <= 64) return B200_SKP(64);
+    if (M <= 128) return B200_SKP(128);
+    return B200_SKP(256);
+#undef B200_SKP
+  }
   const bool two = skinny_stream_tiles(M) == 2;
   if (M <= 16) return two ? B200_SKS(16, 2) : B200_SKS(16, 1);
   if (M <= 32) return two ? B200_SKS(32, 2) : B200_SKS(32, 1);
@@ -1069,11 +1099,12 @@ int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int l
   // stream-K kernel.
   const int mode = skinny_mode();
   // (a forced slice count, b200_gemm_set_splits, takes the split-K kernels)
-  if (epi == nullptr && (mode == 3 || (mode == 1 && skinny_use_stream(M, N, K)))) {
+  const bool pair = mode == 4 || (mode == 1 && skinny_use_pair_stream(M, N, K));
+  if (epi == nullptr && (mode == 3 || pair || (mode == 1 && skinny_use_stream(M, N, K)))) {
     switch (skinny_slabs()) {
-      case 1: return run_skinny_stream_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, scratch);
-      case 4: return run_skinny_stream_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, scratch);
-      default: return run_skinny_stream_slabs<2>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, scratch);
+      case 1: return run_skinny_stream_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, scratch, pair);
+      case 4: return run_skinny_stream_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, scratch, pair);
+      default: return run_skinny_stream_slabs<2>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, scratch, pair);
     }
   }
   // (The cluster kernel writes C directly, so fused epilogues take the
@@ -1116,13 +1147,17 @@ int skinny_slices(int M, int N, int K, const DeviceState* d) {
     return 1;
   }
   const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-  if (mode == 3 || (mode == 1 && skinny_use_stream(M, N, K))) {
-    // stream-K: the most CTAs any one tile of B is cut between
-    const int st = skinny_stream_tiles(M);
-    const long long kb = ceil_div(K, skinny_fit_slabs(mp, skinny_slabs(), st) * kSlabK);
+  const bool pair_stream = mode == 4 || (mode == 1 && skinny_use_pair_stream(M, N, K));
+  if (mode == 3 || pair_stream || (mode == 1 && skinny_use_stream(M, N, K))) {
+    // stream-K: the most CTAs (pairs) any one tile of B is cut between
+    const bool pair = pair_stream;
+    const int st = pair ? 2 : skinny_stream_tiles(M);
+    const int pmp = pair && mp < 32 ? 32 : mp;
+    const long long kb = ceil_div(K, skinny_fit_slabs(pmp, skinny_slabs(), pair ? 1 : st) * kSlabK);
     const long long stiles = ceil_div(N, 128LL * st);
     const long long total = stiles * kb;
-    const int G = (int)(total < (d ? d->sms : 148) ? total : (d ? d->sms : 148));
+    const int workers = (d ? d->sms : 148) / (pair ? 2 : 1);
+    const int G = (int)(total < workers ? total : workers);
     long long most = 1;
     for (long long t = 0; t < stiles; ++t) {
       const long long c = stream_owner_host(t * kb + kb - 1, total, G) -
@@ -1653,7 +1688,7 @@ int b200_gemm_set_skinny_tiles(int tiles) {
 }
 
 int b200_gemm_set_skinny_mode(int mode) {
-  if (mode < 0 || mode > 3) return B200_ERR_INVALID_ARGUMENT;
+  if (mode < 0 || mode > 4) return B200_ERR_INVALID_ARGUMENT;
   g_skinny.store(mode);
   return B200_OK;
 }

@@ -38,17 +38,21 @@ __device__ __forceinline__ int skinny_kb(int kb0, int len, int i, int t, int T) 
 // of B but re-reads A's slab for each unit, and each SM's inflow is the
 // limit in this HBM-bound regime, so a unit of kTiles blocks sharing one A
 // slab per K step cuts A's share of the inflow kTiles-fold.
-template <int kMp, int kSlabs, int kTiles = 1>
+// kPair: 2-CTA pairs (stream-K kernel only): the pair MMA is M = 256 rows of
+// B (128 per CTA) by N = Mp rows of A, and each CTA holds Mp / 2 of A's rows.
+template <int kMp, int kSlabs, int kTiles = 1, bool kPair = false>
 struct SkinnyCfg {
   static_assert(kMp % 16 == 0 && kMp >= 16 && kMp <= 256, "MMA N must be 16..256, step 16");
   static_assert(kTiles * kMp <= 512, "an accumulator of kTiles x Mp columns exceeds TMEM");
+  static_assert(!kPair || (kTiles == 1 && kMp >= 32), "pairs: one block per CTA, Mp >= 32");
   // Two accumulators (the epilogue of one unit overlaps the next unit's
   // MMAs) when they fit in TMEM's 512 columns, else one.
   static constexpr int kAccBufs = 2 * kTiles * kMp <= 512 ? 2 : 1;
   static constexpr int kRowsB = 128;                       // MMA M: rows of B per block
   static constexpr int kBK = kSlabs * kSlabK;              // K per stage
   static constexpr int kSlabB = kRowsB * kSlabK * 2;       // 16 KiB
-  static constexpr int kSlabA = kMp * kSlabK * 2;
+  static constexpr int kRowsA = kPair ? kMp / 2 : kMp;     // rows of A per CTA
+  static constexpr int kSlabA = kRowsA * kSlabK * 2;
   static constexpr int kBytesB = kTiles * kSlabs * kSlabB;
   static constexpr int kBytesA = kSlabs * kSlabA;
   static constexpr int kStageBytes = kBytesB + kBytesA;
@@ -532,13 +536,21 @@ __device__ __forceinline__ int stream_owner(long long x, long long total, int G)
   return (int)(((x + 1) * G + total - 1) / total) - 1;
 }
 
-template <int kMp, int kSlabs, int kTiles = 1>
+// kPair (launched in 2-CTA clusters): a tile is 256 rows of B, CTA r of the
+// pair loads its own 128 of them and rows [r Mp/2, (r+1) Mp/2) of A, and the
+// pair leader issues tcgen05.mma.cta_group::2 (M = 256, N = Mp), which reads
+// both CTAs' shared memory: each SM streams its rows of B but only half of
+// A's slab, where a single CTA re-reads A's whole slab per 128 rows of B.
+// Each CTA's TMEM holds its own 128 rows x Mp columns, so the epilogue, the
+// slots and the fix-up are the single-CTA kernel's, per CTA half h = 2 t + r
+// of tile t; the ranges of (tile, K block) items are per pair.
+template <int kMp, int kSlabs, int kTiles = 1, bool kPair = false>
 __global__ void __launch_bounds__(192, 1)
 gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 64 x 128
-                          const __grid_constant__ CUtensorMap tmap_a,   // M x K, box 64 x Mp
+                          const __grid_constant__ CUtensorMap tmap_a,   // M x K, box 64 x Mp (pairs: Mp / 2)
                           const __grid_constant__ CUtensorMap tmap_c,   // C bf16 M x N, box 32 x kChunk
                           const SkinnyStreamArgs args) {
-  using P = SkinnyCfg<kMp, kSlabs, kTiles>;
+  using P = SkinnyCfg<kMp, kSlabs, kTiles, kPair>;
   static_assert(P::kAccBufs == 2, "the stream-K kernel double-buffers its accumulator");
   constexpr int kStages = P::kStages;
   constexpr int kChunk = P::kChunk;
@@ -546,7 +558,9 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
   // accumulator is kMpT = kTiles x Mp TMEM columns (block i at i x Mp), read
   // by the epilogue in kMpT / kChunk chunks, kCpb of them per block.
   constexpr int kMpT = kTiles * kMp;
-  constexpr int kTileRows = kTiles * P::kRowsB;
+  constexpr int kTileRows = (kPair ? 2 : kTiles) * P::kRowsB;
+  // rows of B one slot / flag unit covers: a tile, or a pair tile's CTA half
+  constexpr int kUnitRows = kPair ? P::kRowsB : kTileRows;
   constexpr int kCpb = kMp / kChunk;
   extern __shared__ uint8_t smem_raw[];
   __shared__ alignas(8) uint64_t bar_full[kStages];
@@ -559,21 +573,23 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int G = gridDim.x;
-  const long long lo = (long long)blockIdx.x * args.total / G;
-  const long long hi = (long long)(blockIdx.x + 1) * args.total / G;
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const int worker = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // pair or CTA
+  const int G = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const long long lo = (long long)worker * args.total / G;
+  const long long hi = (long long)(worker + 1) * args.total / G;
   const int KB = args.k_blocks;
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t store_base = smem_base + kStages * P::kStageBytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(smem_u32(&bar_full[s]), 1);
+      mbar_init(smem_u32(&bar_full[s]), kPair ? 2 : 1);  // pairs: both CTAs' bytes, in the leader
       mbar_init(smem_u32(&bar_empty[s]), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&bar_acc_full[b]), 1);
-      mbar_init(smem_u32(&bar_acc_empty[b]), 4);
+      mbar_init(smem_u32(&bar_acc_empty[b]), kPair ? 8 : 4);  // every epilogue warp (of the pair)
     }
     mbar_init(smem_u32(&bar_drain), 1);
     abort_word = 0;
@@ -583,11 +599,16 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
     prefetch_tmap(&tmap_c);
   }
   if (warp == 1) {
-    tmem_alloc_1(smem_u32(&tmem_slot), P::kTmemAlloc);
-    tmem_relinquish_1();
+    if constexpr (kPair) {
+      tmem_alloc_pair(smem_u32(&tmem_slot), P::kTmemAlloc);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc_1(smem_u32(&tmem_slot), P::kTmemAlloc);
+      tmem_relinquish_1();
+    }
   }
   tc_fence_before_sync();
-  __syncthreads();
+  if constexpr (kPair) cluster_sync_all(); else __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = tmem_slot;
 
@@ -595,7 +616,7 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
   wctx.status = args.status;
   wctx.timeout_ns = args.timeout_ns;
   wctx.abort_local = smem_u32(&abort_word);
-  wctx.abort_peer = smem_u32(&abort_word);
+  wctx.abort_peer = kPair ? cluster_map(smem_u32(&abort_word), rank ^ 1u) : smem_u32(&abort_word);
 
   // Segments of [lo, hi): tile t, K blocks [kb0, kb1).
 #define B200_FOR_SEGMENTS(...)                                                \
@@ -613,6 +634,7 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
       const uint64_t pol_b = args.l2_hint ? l2_policy_evict_first() : l2_policy_evict_normal();
       const uint64_t pol_a = args.l2_hint ? l2_policy_evict_last() : l2_policy_evict_normal();
       uint32_t stage = 0, phase = 0;
+      uint32_t filled = 0;  // ring slots this producer has filled (pairs: the leader forwards frees)
       bool ok = true;
       B200_FOR_SEGMENTS({
         for (int kb = kb0; ok && kb < kb1; ++kb) {
@@ -621,18 +643,37 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
             break;
           }
           const uint32_t sb = smem_base + stage * P::kStageBytes;
-          const uint32_t fb = smem_u32(&bar_full[stage]);
-          mbar_arrive_expect_tx(fb, P::kStageBytes);
-#pragma unroll
-          for (int i = 0; i < kTiles; ++i)
+          if constexpr (kPair) {
+            // The pair MMA commits a freed slot to the leader's empty barrier
+            // only; the leader's producer passes it on to the peer's.
+            if (rank == 0 && filled >= (uint32_t)kStages)
+              mbar_arrive_cluster(cluster_map(smem_u32(&bar_empty[stage]), 1));
+            ++filled;
+            const uint32_t fb = cluster_map(smem_u32(&bar_full[stage]), 0);
+            mbar_arrive_expect_tx_cluster(fb, P::kStageBytes);
 #pragma unroll
             for (int sl = 0; sl < kSlabs; ++sl)
-              tma_load_2d_hint(sb + (i * kSlabs + sl) * P::kSlabB, &tmap_b,
-                               kb * P::kBK + sl * kSlabK, t * kTileRows + i * P::kRowsB, fb, pol_b);
+              tma_load_2d_pair_hint(sb + sl * P::kSlabB, &tmap_b, kb * P::kBK + sl * kSlabK,
+                                    t * kTileRows + (int)rank * P::kRowsB, fb, pol_b);
 #pragma unroll
-          for (int sl = 0; sl < kSlabs; ++sl)
-            tma_load_2d_hint(sb + P::kBytesB + sl * P::kSlabA, &tmap_a, kb * P::kBK + sl * kSlabK,
-                             0, fb, pol_a);
+            for (int sl = 0; sl < kSlabs; ++sl)
+              tma_load_2d_pair_hint(sb + P::kBytesB + sl * P::kSlabA, &tmap_a,
+                                    kb * P::kBK + sl * kSlabK, (int)rank * P::kRowsA, fb, pol_a);
+          } else {
+            const uint32_t fb = smem_u32(&bar_full[stage]);
+            mbar_arrive_expect_tx(fb, P::kStageBytes);
+#pragma unroll
+            for (int i = 0; i < kTiles; ++i)
+#pragma unroll
+              for (int sl = 0; sl < kSlabs; ++sl)
+                tma_load_2d_hint(sb + (i * kSlabs + sl) * P::kSlabB, &tmap_b,
+                                 kb * P::kBK + sl * kSlabK, t * kTileRows + i * P::kRowsB, fb,
+                                 pol_b);
+#pragma unroll
+            for (int sl = 0; sl < kSlabs; ++sl)
+              tma_load_2d_hint(sb + P::kBytesB + sl * P::kSlabA, &tmap_a,
+                               kb * P::kBK + sl * kSlabK, 0, fb, pol_a);
+          }
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
@@ -640,8 +681,8 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_bf16_f32(P::kRowsB, kMp);
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = make_idesc_bf16_f32(kPair ? 2 * P::kRowsB : P::kRowsB, kMp);
       uint32_t stage = 0, phase = 0;
       int it = 0;
       bool ok = true;
@@ -666,18 +707,33 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
 #pragma unroll
               for (int i = 0; i < kTiles; ++i) {
                 const uint64_t bdesc = make_sdesc_k128(sb + (i * kSlabs + sl) * P::kSlabB);
-                umma_bf16_1(d_tmem + i * kMp, bdesc + 2ull * k, adesc + 2ull * k, idesc,
-                            (kb != kb0 || sl != 0 || k != 0) ? 1u : 0u);
+                const uint32_t acc = (kb != kb0 || sl != 0 || k != 0) ? 1u : 0u;
+                if constexpr (kPair)
+                  umma_bf16_pair(d_tmem + i * kMp, bdesc + 2ull * k, adesc + 2ull * k, idesc, acc);
+                else
+                  umma_bf16_1(d_tmem + i * kMp, bdesc + 2ull * k, adesc + 2ull * k, idesc, acc);
               }
           }
-          umma_commit_1(smem_u32(&bar_empty[stage]));
+          if constexpr (kPair)
+            umma_commit_pair(cluster_map(smem_u32(&bar_empty[stage]), 0));
+          else
+            umma_commit_1(smem_u32(&bar_empty[stage]));
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        umma_commit_1(smem_u32(&bar_acc_full[buf]));
+        if constexpr (kPair) {
+          umma_commit_pair(cluster_map(smem_u32(&bar_acc_full[buf]), 0));
+          umma_commit_pair(cluster_map(smem_u32(&bar_acc_full[buf]), 1));
+        } else {
+          umma_commit_1(smem_u32(&bar_acc_full[buf]));
+        }
         ++it;
       })
-      umma_commit_1(smem_u32(&bar_drain));
+      // Every MMA this thread issued must finish before TMEM is freed.
+      if constexpr (kPair)
+        umma_commit_pair(cluster_map(smem_u32(&bar_drain), 0));
+      else
+        umma_commit_1(smem_u32(&bar_drain));
       if (!mbar_try_wait(smem_u32(&bar_drain), 0))
         wait_slow(smem_u32(&bar_drain), 0, wctx, kErrWaitDrain, false);
     }
@@ -710,7 +766,7 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_store_2d(&tmap_c, sb, t * kTileRows + (c / kCpb) * P::kRowsB + q * 32,
+        tma_store_2d(&tmap_c, sb, t * kUnitRows + (c / kCpb) * P::kRowsB + q * 32,
                      (c % kCpb) * kChunk);
         bulk_commit_group();
       }
@@ -729,8 +785,10 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
       const uint32_t tbase = tmem_base + buf * kMpT + ((uint32_t)(quarter * 32) << 16);
       const bool whole = kb0 == 0 && kb1 == KB;
       const int first = stream_owner((long long)t * KB, args.total, G);
-      const int j = (int)blockIdx.x - first;
-      float* slot = args.slots + ((long long)t * args.max_seg + j) * kMpT * P::kRowsB +
+      const int j = worker - first;
+      // slot / flag unit: the tile, or this CTA's half of a pair tile
+      const int h = kPair ? 2 * t + (int)rank : t;
+      float* slot = args.slots + ((long long)h * args.max_seg + j) * kMpT * P::kRowsB +
                     quarter * kMpT * 32 + lane;
 #pragma unroll 1
       for (int c = 0; c < kMpT / kChunk; ++c) {
@@ -743,10 +801,15 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
         if (c == kMpT / kChunk - 1) {
           tc_fence_before_sync();
           __syncwarp();
-          if (lane == 0) mbar_arrive_local(smem_u32(&bar_acc_empty[buf]));
+          if (lane == 0) {
+            if constexpr (kPair)
+              mbar_arrive_cluster(cluster_map(smem_u32(&bar_acc_empty[buf]), 0));
+            else
+              mbar_arrive_local(smem_u32(&bar_acc_empty[buf]));
+          }
         }
         if (whole) {
-          store_bf16(v, t, quarter, c);
+          store_bf16(v, h, quarter, c);
         } else {
           // slot[quarter][m][lane]: each warp-wide store covers 128 contiguous bytes
 #pragma unroll
@@ -761,11 +824,11 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
           asm volatile("fence.acq_rel.gpu;" ::: "memory");
           __syncwarp();
           if (lane == 0)
-            st_release_gpu_u32(args.flags + ((long long)t * args.max_seg + j) * 4 + quarter,
+            st_release_gpu_u32(args.flags + ((long long)h * args.max_seg + j) * 4 + quarter,
                                args.epoch);
         }
         if (nfix < 2) {
-          fix_t[nfix] = t;
+          fix_t[nfix] = h;
           fix_j[nfix] = j;
           fix_n[nfix] = n;
           ++nfix;
@@ -870,7 +933,7 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
       __syncwarp();
       if (lane == 0) {
         tma_store_2d(&tmap_c, sb,
-                     fix_t[f] * kTileRows + ((pc >> 2) / kCpb) * P::kRowsB + (pc & 3) * 32,
+                     fix_t[f] * kUnitRows + ((pc >> 2) / kCpb) * P::kRowsB + (pc & 3) * 32,
                      ((pc >> 2) % kCpb) * kChunk);
         bulk_commit_group();
       }
@@ -925,11 +988,15 @@ gemm_skinny_stream_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K
 #undef B200_FOR_SEGMENTS
 
   tc_fence_before_sync();
-  __syncthreads();
+  if constexpr (kPair) cluster_sync_all(); else __syncthreads();
   if (warp == 1) {
     tc_fence_after_sync();
-    tmem_dealloc_1(tmem_base, P::kTmemAlloc);
+    if constexpr (kPair)
+      tmem_dealloc_pair(tmem_base, P::kTmemAlloc);
+    else
+      tmem_dealloc_1(tmem_base, P::kTmemAlloc);
   }
+  if constexpr (kPair) cluster_sync_all();
 }
 
 }  // namespace b200

@@ -181,13 +181,14 @@ def test_k_split_and_row_shard_on_two_gpus():
 
 
 # ------------------------------------------------------- skinny-M kernel
-SKINNY_MODES = {"auto": 1, "cluster": 2, "stream": 3}
+SKINNY_MODES = {"auto": 1, "cluster": 2, "stream": 3, "pair_stream": 4}
 
 
 @pytest.fixture(params=list(SKINNY_MODES))
 def skinny_mode(request):
-    """The skinny path's kernels: chosen per shape, the cluster split-K kernel
-    and the stream-K kernel, each forced for every M."""
+    """The skinny path's kernels: chosen per shape, the cluster split-K kernel,
+    the stream-K kernel and the stream-K kernel on 2-CTA pairs, each forced for
+    every M."""
     capi.set_skinny_mode(SKINNY_MODES[request.param])
     yield request.param
     capi.set_skinny_mode(1)
@@ -218,15 +219,16 @@ def test_skinny_kernel_forced_splits_random(splits):
     assert parity.passes(parity.metrics(C, A.float() @ Bt.float().T, A, Bt))
 
 
+@pytest.mark.parametrize("mode", [3, 4], ids=["cta", "pair"])
 @pytest.mark.parametrize("M,N,K", [(128, 24576, 1024), (128, 12288, 1024), (100, 4096, 2048),
-                                   (256, 8192, 1024), (64, 1024, 8192)])
-def test_skinny_stream_k_fixup_exact_bits(M, N, K):
-    """The stream-K skinny kernel over its fix-up structures: blocks of B
-    split between two CTAs (the second finishes the block alone), between
-    three to six (every contributor finishes a share), mixtures of both, and
-    about twenty contributors to a block (more than its pieces, so some
-    contributors finish nothing)."""
-    capi.set_skinny_mode(3)
+                                   (256, 8192, 1024), (64, 1024, 8192), (32, 2048, 16384)])
+def test_skinny_stream_k_fixup_exact_bits(M, N, K, mode):
+    """The stream-K skinny kernel (one CTA, or 2-CTA pairs) over its fix-up
+    structures: blocks of B split between two workers (the second finishes
+    the block alone), between three to six (every contributor finishes a
+    share), mixtures of both, and about twenty contributors to a block (more
+    than its pieces, so some contributors finish nothing)."""
+    capi.set_skinny_mode(mode)
     try:
         A, Bt = oracle.exact_inputs(M, N, K, seed=M + N)
         C = bf16_gemm(dev(A), dev(Bt))
@@ -292,3 +294,14 @@ def test_skinny_stream_k_tiles_exact_bits(M, N, K, tiles):
     finally:
         capi.set_skinny_mode(1)
         capi.set_skinny_tiles(0)
+
+
+@pytest.mark.parametrize("M,N,K", [(200, 24576, 1024), (256, 16384, 2048)])
+def test_skinny_wide_n_takes_pair_stream_k_exact_bits(M, N, K):
+    """Above M = 128 with an fp32 workspace of 16 MB or more, the per-shape
+    choice runs the stream-K kernel on 2-CTA pairs: exact results there."""
+    capi.set_skinny_mode(1)
+    A, Bt = oracle.exact_inputs(M, N, K, seed=M + 3)
+    C = bf16_gemm(dev(A), dev(Bt))
+    assert np.array_equal(bits(C), oracle.gemm_bf16(A, Bt))
+    assert capi.device_status(True) == 0
