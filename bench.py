@@ -851,6 +851,11 @@ def run_sweep(args, world, rank, dev):
         groups = [("skinny" if M <= 256 else "shape", [(M, N, K)]) for M, N, K in custom]
     else:
         groups = [(name, CONFIGS[name]) for name in ("square_1024", "square", "projection", "skinny")]
+    # What any kernel costs under this protocol: a one-block add after the
+    # flush (launch and completion), reported beside the small shapes.
+    tiny = torch.zeros(16, device=dev)
+    floor_us = statistics.median(time_cold(lambda: tiny.add_(1), steps, args.warmup, stream,
+                                           flush)) * 1e3
     for name, shapes in groups:
         for (M, N, K) in shapes:
             std = WEIGHT_STD.get(name, WEIGHT_STD["skinny"] if M <= 256 else WEIGHT_STD["square"])
@@ -880,6 +885,15 @@ def run_sweep(args, world, rank, dev):
             tf = lambda ms: fl / (ms * 1e-3) / 1e12
             hbm = name == "skinny"
             achieved = by / (ours * 1e-3) / 1e9 if hbm else tf(ours)
+            probe = None
+            if hbm:
+                # A plain read of B's N x K bf16 (torch's sum, fp32 accumulation)
+                # under the same protocol: the HBM rate a library kernel gets for
+                # these bytes after the flush, launch and completion included.
+                pr = med(lambda: Bt.sum(dtype=torch.float32))
+                probe = {"what": "torch sum over B (N x K bf16), same protocol",
+                         "us": pr * 1e3, "gbs": 2 * N * K / (pr * 1e-3) / 1e9,
+                         "ours_vs_probe": pr / ours}
             print(json.dumps({
                 "config": name, "M": M, "N": N, "K": K, "ours_us": ours * 1e3,
                 "ours_tflops": tf(ours), "cublas_tflops": tf(cub),
@@ -894,6 +908,8 @@ def run_sweep(args, world, rank, dev):
                              "unit": "GB/s" if hbm else "TFLOP/s",
                              "frac": achieved / (peak_gbs if hbm else peak_tf),
                              "peak_source": src},
+                "hbm_read_probe": probe,
+                "launch_floor_us": floor_us,
                 "parity": par, "timing": f"median of {steps} cold-L2 launches (256 MB flush "
                                           "between), same process, 1 s idle before each arm",
             }), flush=True)

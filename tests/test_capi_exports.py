@@ -121,3 +121,42 @@ def test_ksplit_rejects_bad_arguments_without_a_device():
     assert lib.b200_ksplit_connect(None, None) == capi.ERR_INVALID_ARGUMENT
     assert lib.b200_ksplit_destroy(None) == capi.OK
     assert capi.KSPLIT_HANDLE_BYTES == 128
+
+
+def test_mode_setters_accept_their_range_and_reject_the_rest():
+    lib = capi.lib()
+    for mode in range(5):                       # 4: stream-K on 2-CTA pairs
+        assert lib.b200_gemm_set_skinny_mode(mode) == capi.OK
+    assert lib.b200_gemm_set_skinny_mode(5) == capi.ERR_INVALID_ARGUMENT
+    assert lib.b200_gemm_set_skinny_mode(-1) == capi.ERR_INVALID_ARGUMENT
+    capi.set_skinny_mode(1)
+    for tiles in (0, 1, 2):
+        assert lib.b200_gemm_set_skinny_tiles(tiles) == capi.OK
+    assert lib.b200_gemm_set_skinny_tiles(3) == capi.ERR_INVALID_ARGUMENT
+    capi.set_skinny_tiles(0)
+    for mode in (0, 1):
+        assert lib.b200_gemm_set_dynamic(mode) == capi.OK
+    assert lib.b200_gemm_set_dynamic(2) == capi.ERR_INVALID_ARGUMENT
+    capi.set_dynamic(0)
+
+
+def test_skinny_slice_reports_follow_the_kernel_choice():
+    # Without a device the launcher assumes 148 SMs; the per-shape choice is
+    # plain integer arithmetic: one-CTA stream-K up to M = 128, the pair
+    # stream-K kernel above it where the split-K workspace reaches 16 MB.
+    capi.set_skinny_mode(1)
+    capi.set_splits(0)
+    wide = capi.get_splits(256, 28672, 4096)           # pair stream-K: contributors per tile
+    narrow = capi.get_splits(256, 8192, 8192)          # split-K kernel: K slices
+    assert wide >= 1 and narrow >= 1
+    capi.set_skinny_mode(4)
+    assert capi.get_splits(256, 28672, 4096) == wide   # forcing the pair kernel changes nothing
+    capi.set_skinny_mode(1)
+
+
+def test_noalloc_status_needs_a_device():
+    v = ctypes.c_int(7)
+    assert capi.lib().b200_gemm_noalloc_status(1, None) == capi.ERR_INVALID_ARGUMENT
+    st = capi.lib().b200_gemm_noalloc_status(1, ctypes.byref(v))
+    assert st in (capi.OK, capi.ERR_UNSUPPORTED_DEVICE)   # no GPU here: refused, not crashed
+    assert capi.noalloc_wait_probe(0) == capi.ERR_INVALID_ARGUMENT
