@@ -189,6 +189,32 @@ def time_cold(fn, steps, warmup, stream, flush):
     return [a.elapsed_time(b) for a, b in zip(s, e)]
 
 
+def time_clean(fn, steps, warmup, stream, flush, clean):
+    """As time_cold, but the zero-write of the flush buffer is followed by a
+    read of a second buffer larger than L2, so the timed call starts with an
+    L2 that holds neither its operands nor dirty lines.  (After the write
+    alone, up to the whole L2 is dirty and the timed call pays for writing it
+    back: at the HBM-bound shapes that halves the apparent read rate.)"""
+    def clean_flush():
+        flush.zero_()
+        clean.sum()
+    torch.cuda.synchronize()
+    time.sleep(IDLE_BEFORE_ARM_S)
+    for _ in range(warmup):
+        clean_flush()
+        fn()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        clean_flush()
+        starts[i].record(stream)
+        fn()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in zip(starts, ends)]
+
+
 # ------------------------------------------------------------------- arms
 def gemm_ours(A, Bt, C, stream):
     """The product call the bench times: the C ABI on device pointers."""
@@ -844,6 +870,7 @@ def run_sweep(args, world, rank, dev):
     peak_tf = float(peaks.get("bf16_tflops", FALLBACK_BF16_TFLOPS))
     peak_gbs = float(peaks.get("hbm_gbs", 6650.0))
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    clean = torch.ones(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
     steps = max(10, min(args.steps, 50))
     if args.shapes:
@@ -885,7 +912,7 @@ def run_sweep(args, world, rank, dev):
             tf = lambda ms: fl / (ms * 1e-3) / 1e12
             hbm = name == "skinny"
             achieved = by / (ours * 1e-3) / 1e9 if hbm else tf(ours)
-            probe = None
+            probe = clean_l2 = None
             if hbm:
                 # A plain read of B's N x K bf16 (torch's sum, fp32 accumulation)
                 # under the same protocol: the HBM rate a library kernel gets for
@@ -894,6 +921,17 @@ def run_sweep(args, world, rank, dev):
                 probe = {"what": "torch sum over B (N x K bf16), same protocol",
                          "us": pr * 1e3, "gbs": 2 * N * K / (pr * 1e-3) / 1e9,
                          "ours_vs_probe": pr / ours}
+                # The same three calls after a flush that leaves L2 clean.
+                cmed = lambda fn: statistics.median(
+                    time_clean(fn, steps, args.warmup, stream, flush, clean))
+                c_ours = cmed(lambda: gemm_ours(A, Bt, C, stream))
+                c_cub = cmed(lambda: torch.matmul(A, Bt.T))
+                c_pr = cmed(lambda: Bt.sum(dtype=torch.float32))
+                clean_l2 = {"flush": "256 MB written, then another 256 MB read",
+                            "ours_us": c_ours * 1e3, "cublas_us": c_cub * 1e3,
+                            "sum_b_us": c_pr * 1e3, "ours_vs_cublas": c_cub / c_ours,
+                            "ours_gbs": by / (c_ours * 1e-3) / 1e9,
+                            "ours_frac": by / (c_ours * 1e-3) / 1e9 / peak_gbs}
             print(json.dumps({
                 "config": name, "M": M, "N": N, "K": K, "ours_us": ours * 1e3,
                 "ours_tflops": tf(ours), "cublas_tflops": tf(cub),
@@ -909,6 +947,7 @@ def run_sweep(args, world, rank, dev):
                              "frac": achieved / (peak_gbs if hbm else peak_tf),
                              "peak_source": src},
                 "hbm_read_probe": probe,
+                "clean_l2": clean_l2,
                 "launch_floor_us": floor_us,
                 "parity": par, "timing": f"median of {steps} cold-L2 launches (256 MB flush "
                                           "between), same process, 1 s idle before each arm",
