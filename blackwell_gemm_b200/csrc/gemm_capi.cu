@@ -161,12 +161,13 @@ int skinny_stream_tiles(int M) {
 }
 
 // Skinny-M path (M <= 256): 0 = off, 1 = chosen per shape, 2 = the cluster
-// kernel for every M, 3 = the stream-K kernel for every M.  Initialised from
-// B200_GEMM_SKINNY, changeable through b200_gemm_set_skinny_mode.
+// kernel for every M, 3 = the stream-K kernel for every M, 4 = the stream-K
+// kernel on 2-CTA pairs, 5 = the cluster kernel on 2-CTA pairs.  Initialised
+// from B200_GEMM_SKINNY, changeable through b200_gemm_set_skinny_mode.
 int skinny_mode() {
   int v = g_skinny.load();
   if (v < 0) {
-    v = env_int("B200_GEMM_SKINNY", 1, 0, 4);
+    v = env_int("B200_GEMM_SKINNY", 1, 0, 5);
     g_skinny.store(v);
   }
   return v;
@@ -303,17 +304,21 @@ bool set_skinny_limits() {
   return set_skinny_limits_for<1>() && set_skinny_limits_for<2>() && set_skinny_limits_for<4>();
 }
 
-// Skinny cluster kernels: (Mp, ring depth) per slot of DeviceState::sk_clusters.
-// Shallow rings let two CTAs share an SM, deep ones keep one CTA per SM.
-constexpr int kSkc[][2] = {{16, 5}, {16, 10}, {32, 3}, {32, 9}, {64, 3}, {64, 8}, {128, 6},
-                           {256, 4}};
-constexpr int kNumSkc = 8;
+// Skinny cluster kernels: (Mp, ring depth, pair slices) per slot of
+// DeviceState::sk_clusters.  Shallow rings let two CTAs share an SM, deep
+// ones keep one CTA per SM; slots 8-11 are the 2-CTA-pair kernels.
+constexpr int kSkc[][3] = {{16, 5, 0},  {16, 10, 0}, {32, 3, 0},  {32, 9, 0},
+                           {64, 3, 0},  {64, 8, 0},  {128, 6, 0}, {256, 4, 0},
+                           {32, 10, 1}, {64, 9, 1},  {128, 8, 1}, {256, 6, 1}};
+constexpr int kNumSkc = 12;
+constexpr int kSkcPair0 = 8;  // first pair slot
 
 template <int I>
 struct Skc {
   static constexpr int kMp = kSkc[I][0], kStages = kSkc[I][1];
-  using P = SkinnyClusterCfg<kMp, kStages>;
-  static constexpr auto kernel = gemm_skinny_cluster_kernel<kMp, kStages>;
+  static constexpr bool kPair = kSkc[I][2] != 0;
+  using P = SkinnyClusterCfg<kMp, kStages, kPair>;
+  static constexpr auto kernel = gemm_skinny_cluster_kernel<kMp, kStages, kPair>;
 };
 
 template <int I>
@@ -322,7 +327,7 @@ bool skc_init(DeviceState& d) {
   if (cudaFuncSetAttribute(S::kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            S::P::kSmemBytes) != cudaSuccess)
     return false;
-  for (int ci = 0; ci < 4; ++ci) {
+  for (int ci = S::kPair ? 1 : 0; ci < 4; ++ci) {  // pairs: clusters of 2, 4, 8
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(8 * d.sms, 1, 1);
     cfg.blockDim = dim3(S::P::kThreads, 1, 1);
@@ -346,7 +351,8 @@ bool skc_init(DeviceState& d) {
 
 bool skc_init_all(DeviceState& d) {
   return skc_init<0>(d) && skc_init<1>(d) && skc_init<2>(d) && skc_init<3>(d) &&
-         skc_init<4>(d) && skc_init<5>(d) && skc_init<6>(d) && skc_init<7>(d);
+         skc_init<4>(d) && skc_init<5>(d) && skc_init<6>(d) && skc_init<7>(d) &&
+         skc_init<8>(d) && skc_init<9>(d) && skc_init<10>(d) && skc_init<11>(d);
 }
 
 int init_device(DeviceState& d, int dev) {
@@ -779,11 +785,57 @@ int choose_skinny_splits(long long tiles, int k_blocks, int ctas, int M, int N, 
 
 constexpr int kSkinnyMaxM = 256;
 
-// Rows of A up to which the cluster kernel is chosen: 8, or 16 while B is
-// under 32 M elements (measured crossovers against the stream-K kernel at
-// N = K = 4096 and 8192).
-bool skinny_use_cluster(int M, int N, int K) {
-  return M <= 8 || (M <= 16 && (long long)N * K < (32LL << 20));
+int skinny_occupancy();
+int skc_choose(const DeviceState& d, int I, bool pair, long long tiles, int k_blocks);
+
+// Cluster-kernel slot (kSkc) that run_skinny_cluster takes for M rows of A
+// with one-CTA slices.
+int skc_slot(int M) {
+  const bool two = skinny_occupancy() == 2;
+  return M <= 16 ? (two ? 0 : 1) : M <= 32 ? (two ? 2 : 3) : M <= 64 ? (two ? 4 : 5)
+                                                            : M <= 128 ? 6 : 7;
+}
+
+// The cluster kernel (mode 1) up to M = 128 where its grid of 128-row blocks
+// x S slices fits in one wave and each CTA's slice, (128 + Mp) rows of B and
+// A over K / S, stays within kClusterMaxSliceBytes.  It ends with one
+// distributed-shared-memory reduction (~1 us) where the stream-K kernel ends
+// with a global-memory fix-up of the blocks split between CTAs (~4 us), but
+// it streams with the CTAs of whole clusters (128 at N = 8192 or 4096)
+// rather than every SM, so it wins while slices are short.  Measured (cold
+// L2, median us, cluster / stream-K; after a written flush and after a flush
+// that leaves L2 clean): N = K = 8192: M = 16 (1.18 MB) 34.9 / 36.3, 31.8 /
+// 32.3; M = 32 (1.31 MB) 36.9 / 36.2, 33.6 / 33.0; M = 64 36.9 / 36.1 at best;
+// N = K = 4096: M = 32 18.5 / 21.8, 16.5 / 19.9; M = 64 20.6 / 22.1, 18.6 /
+// 21.8; M = 128 24.8 / 26.1, 24.5 / 24.7; N = 4096, K = 14336, M = 128 (1.8
+// MB) 39.5 / 39.8, 36.9 / 38.2.  With a forced slice count
+// (b200_gemm_set_splits) only M <= 8 takes it, as the split-K kernels do.
+constexpr double kClusterMaxSliceBytes = 1.2e6;
+
+bool skinny_use_cluster(int M, int N, int K, const DeviceState* d) {
+  if (tuning_splits() > 0) return M <= 8;
+  if (M > 128) return false;
+  const int I = skc_slot(M);
+  const long long tiles = ceil_div(N, 128);
+  const int k_blocks = (int)ceil_div(K, kSlabK);
+  int ci = 0;
+  long long fit = 0;
+  if (d != nullptr) {
+    ci = skc_choose(*d, I, false, tiles, k_blocks);
+    fit = d->sk_clusters[I][ci];
+  } else {
+    // no device: 148 SMs, one CTA each (GPC limits ignored)
+    for (int c = 3; c >= 1; --c)
+      if (tiles <= (148 >> c) && k_blocks >= (8 << c)) {
+        ci = c;
+        break;
+      }
+    fit = 148 >> ci;
+  }
+  if (tiles > fit) return false;
+  const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  const double slice = (128.0 + mp) * 2.0 * kSlabK * (double)ceil_div(k_blocks, 1 << ci);
+  return slice <= kClusterMaxSliceBytes;
 }
 
 // Per shape (mode 1), without a forced slice count: the stream-K kernel
@@ -791,8 +843,8 @@ bool skinny_use_cluster(int M, int N, int K) {
 // persistent split-K kernel there at N, K = 4096..28672), the split-K kernel
 // above (its units of two blocks of B share A's slab; the stream-K kernel
 // re-reads A per block, twice B's bytes at M = 256).
-bool skinny_use_stream(int M, int N, int K) {
-  return tuning_splits() == 0 && !skinny_use_cluster(M, N, K) && M <= 128;
+bool skinny_use_stream(int M, int N, int K, const DeviceState* d) {
+  return tuning_splits() == 0 && !skinny_use_cluster(M, N, K, d) && M <= 128;
 }
 
 // Above M = 128, the stream-K kernel on 2-CTA pairs where the split-K
@@ -803,8 +855,7 @@ bool skinny_use_stream(int M, int N, int K) {
 // 41.4.  At M <= 128 the pair kernel was ~2 us slower than the one-CTA
 // stream-K kernel at every shape (the pair TMEM allocation's launch cost).
 bool skinny_use_pair_stream(int M, int N, int K) {
-  return tuning_splits() == 0 && M > 128 && (long long)M * N >= (4LL << 20) &&
-         !skinny_use_cluster(M, N, K);
+  return tuning_splits() == 0 && M > 128 && (long long)M * N >= (4LL << 20);
 }
 
 template <int kMp, int kSlabsWanted>
@@ -1012,32 +1063,39 @@ int skinny_slabs() {
   return s;
 }
 
-// Cluster split-K: the largest cluster (8, 4, 2, 1) whose grid of
-// tiles x S CTAs fits in one wave, keeping >= 8 K-blocks per rank.
+// Cluster split-K: the largest cluster (8, 4, 2, 1 CTAs; pair kernels 8, 4,
+// 2) whose grid of tiles x cluster-size CTAs fits in one wave, keeping >= 8
+// K blocks per slice; a forced slice count (b200_gemm_set_splits) picks the
+// cluster whose slice count is the largest power of two not above it.
+// Returns log2 of the cluster size.
+int skc_choose(const DeviceState& d, int I, bool pair, long long tiles, int k_blocks) {
+  const int lo = pair ? 1 : 0;
+  const int forced = tuning_splits();
+  if (forced > 0) {
+    int ci = lo;
+    while (ci < 3 && ((2 << ci) >> lo) <= forced) ++ci;
+    return ci;
+  }
+  for (int c = 3; c > lo; --c) {
+    const long long clusters = d.sk_clusters[I][c];
+    if (clusters > 0 && tiles <= clusters && k_blocks >= 8 * ((1 << c) >> lo)) return c;
+  }
+  return lo;
+}
+
 template <int I>
 int launch_skinny_cluster(const void* A, const void* B, void* C, int M, int N, int K, int lda,
                           int ldb, int ldc, DeviceState& d, cudaStream_t stream) {
   using S = Skc<I>;
-  const long long tiles = ceil_div(N, S::P::kRowsB);
+  const long long tiles = ceil_div(N, S::P::kBlockRows);
   const int k_blocks = (int)ceil_div(K, kSlabK);
-  int ci = 0;
-  const int forced = tuning_splits();
-  if (forced > 0) {
-    while (ci < 3 && (2 << ci) <= forced) ++ci;
-  } else {
-    for (int c = 3; c >= 1; --c) {
-      const long long clusters = d.sk_clusters[I][c];
-      if (clusters > 0 && tiles <= clusters && k_blocks >= 8 * (1 << c)) {
-        ci = c;
-        break;
-      }
-    }
-  }
+  const int ci = skc_choose(d, I, S::kPair, tiles, k_blocks);
   if (d.sk_clusters[I][ci] < 1) return B200_ERR_LAUNCH;
   const int csize = 1 << ci;
+  const int slices = S::kPair ? csize / 2 : csize;
   CUtensorMap tb, ta;
   if (encode_2d(&tb, B, K, N, ldb, kSlabK, S::P::kRowsB) != B200_OK ||
-      encode_2d(&ta, A, K, M, lda, kSlabK, S::kMp) != B200_OK)
+      encode_2d(&ta, A, K, M, lda, kSlabK, S::P::kRowsA) != B200_OK)
     return B200_ERR_TENSOR_MAP;
   SkinnyClusterArgs args;
   args.l2_hint = skinny_l2_hint();
@@ -1045,7 +1103,7 @@ int launch_skinny_cluster(const void* A, const void* B, void* C, int M, int N, i
   args.N = N;
   args.K = K;
   args.k_blocks = k_blocks;
-  args.kb_per = (int)ceil_div(k_blocks, csize);
+  args.kb_per = (int)ceil_div(k_blocks, slices);
   args.ldc = ldc;
   args.C = static_cast<__nv_bfloat16*>(C);
   args.status = d.status;
@@ -1077,30 +1135,39 @@ int skinny_occupancy() {
 }
 
 int run_skinny_cluster(const void* A, const void* B, void* C, int M, int N, int K, int lda,
-                       int ldb, int ldc, DeviceState& d, cudaStream_t stream) {
-  const bool two = skinny_occupancy() == 2;
+                       int ldb, int ldc, DeviceState& d, cudaStream_t stream, bool pair = false) {
 #define B200_SKC(I) launch_skinny_cluster<I>(A, B, C, M, N, K, lda, ldb, ldc, d, stream)
-  if (M <= 16) return two ? B200_SKC(0) : B200_SKC(1);
-  if (M <= 32) return two ? B200_SKC(2) : B200_SKC(3);
-  if (M <= 64) return two ? B200_SKC(4) : B200_SKC(5);
-  if (M <= 128) return B200_SKC(6);
-  return B200_SKC(7);
+  if (pair) {
+    if (M <= 32) return B200_SKC(kSkcPair0);
+    if (M <= 64) return B200_SKC(kSkcPair0 + 1);
+    if (M <= 128) return B200_SKC(kSkcPair0 + 2);
+    return B200_SKC(kSkcPair0 + 3);
+  }
+  switch (skc_slot(M)) {
+    case 0: return B200_SKC(0);
+    case 1: return B200_SKC(1);
+    case 2: return B200_SKC(2);
+    case 3: return B200_SKC(3);
+    case 4: return B200_SKC(4);
+    case 5: return B200_SKC(5);
+    case 6: return B200_SKC(6);
+    default: return B200_SKC(7);
+  }
 #undef B200_SKC
 }
 
 int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
                int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi = nullptr,
                const Scratch* scratch = nullptr) {
-  // Per shape (mode 1): for the fewest rows of A (skinny_use_cluster) the
-  // single-launch cluster kernel (A's box is then mostly out of bounds, so
-  // nearly only B streams); up to 128 rows the stream-K kernel (all SMs, no
-  // workspace clear or rounding pass); above, the persistent split-K kernel.
-  // B200_GEMM_SKINNY=2 forces the cluster kernel for every M, 3 the
-  // stream-K kernel.
+  // Per shape (mode 1), up to 128 rows of A: the single-launch cluster
+  // kernel where its slices are short (skinny_use_cluster), else the
+  // stream-K kernel (all SMs, no workspace clear or rounding pass); above,
+  // the stream-K kernel on 2-CTA pairs for wide B, else the persistent
+  // split-K kernel.  B200_GEMM_SKINNY = 2..5 forces one kernel for every M.
   const int mode = skinny_mode();
   // (a forced slice count, b200_gemm_set_splits, takes the split-K kernels)
   const bool pair = mode == 4 || (mode == 1 && skinny_use_pair_stream(M, N, K));
-  if (epi == nullptr && (mode == 3 || pair || (mode == 1 && skinny_use_stream(M, N, K)))) {
+  if (epi == nullptr && (mode == 3 || pair || (mode == 1 && skinny_use_stream(M, N, K, &d)))) {
     switch (skinny_slabs()) {
       case 1: return run_skinny_stream_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, scratch, pair);
       case 4: return run_skinny_stream_slabs<4>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, scratch, pair);
@@ -1109,7 +1176,9 @@ int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int l
   }
   // (The cluster kernel writes C directly, so fused epilogues take the
   // workspace kernel, whose rounding pass applies them.)
-  if (epi == nullptr && (mode == 2 || skinny_use_cluster(M, N, K)))
+  if (epi == nullptr && mode == 5)
+    return run_skinny_cluster(A, B, C, M, N, K, lda, ldb, ldc, d, stream, true);
+  if (epi == nullptr && (mode == 2 || (mode == 1 && skinny_use_cluster(M, N, K, &d))))
     return run_skinny_cluster(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
   switch (skinny_slabs()) {
     case 1: return run_skinny_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi, scratch);
@@ -1131,24 +1200,15 @@ int skinny_slices(int M, int N, int K, const DeviceState* d) {
   const int mode = skinny_mode();
   const int forced = tuning_splits();
   const long long tiles = ceil_div(N, 128);
-  if (d && (mode == 2 || (mode == 1 && skinny_use_cluster(M, N, K)))) {
-    const int k_blocks = (int)ceil_div(K, kSlabK);
-    if (forced > 0) {
-      int ci = 0;
-      while (ci < 3 && (2 << ci) <= forced) ++ci;
-      return 1 << ci;
-    }
-    // the ring depth the default occupancy picks for this M (run_skinny_cluster)
-    const int I = M <= 16 ? 1 : M <= 32 ? 3 : M <= 64 ? 5 : M <= 128 ? 6 : 7;
-    for (int c = 3; c >= 1; --c) {
-      const long long clusters = d->sk_clusters[I][c];
-      if (clusters > 0 && tiles <= clusters && k_blocks >= 8 * (1 << c)) return 1 << c;
-    }
-    return 1;
+  if (d && mode == 5) {
+    const int I = kSkcPair0 + (M <= 32 ? 0 : M <= 64 ? 1 : M <= 128 ? 2 : 3);
+    return (1 << skc_choose(*d, I, true, ceil_div(N, 256), (int)ceil_div(K, kSlabK))) / 2;
   }
+  if (d && (mode == 2 || (mode == 1 && skinny_use_cluster(M, N, K, d))))
+    return 1 << skc_choose(*d, skc_slot(M), false, tiles, (int)ceil_div(K, kSlabK));
   const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
   const bool pair_stream = mode == 4 || (mode == 1 && skinny_use_pair_stream(M, N, K));
-  if (mode == 3 || pair_stream || (mode == 1 && skinny_use_stream(M, N, K))) {
+  if (mode == 3 || pair_stream || (mode == 1 && skinny_use_stream(M, N, K, d))) {
     // stream-K: the most CTAs (pairs) any one tile of B is cut between
     const bool pair = pair_stream;
     const int st = pair ? 2 : skinny_stream_tiles(M);
@@ -1688,7 +1748,7 @@ int b200_gemm_set_skinny_tiles(int tiles) {
 }
 
 int b200_gemm_set_skinny_mode(int mode) {
-  if (mode < 0 || mode > 4) return B200_ERR_INVALID_ARGUMENT;
+  if (mode < 0 || mode > 5) return B200_ERR_INVALID_ARGUMENT;
   g_skinny.store(mode);
   return B200_OK;
 }

@@ -306,20 +306,31 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 6
 namespace b200 {
 
 // ---------------------------------------------------------------------------
-// Cluster split-K variant: no workspace, one launch.  A cluster of S CTAs
-// (S = 1, 2, 4 or 8, a launch attribute) owns one 128-row block of B; CTA r
-// of the cluster accumulates K blocks [r * kb_per, (r+1) * kb_per) into its
-// own TMEM.  The S partial sums are then added through distributed shared
-// memory 32 output columns (= rows of C) at a time: every CTA copies its
-// TMEM chunk c into a shared staging slot, the cluster synchronises, CTA
-// (c % S) adds the S slots and writes bf16 C, the cluster synchronises again
-// before the slot is reused.  The grid is not persistent: blocks x S CTAs,
-// one work unit each.
-template <int kMp, int kStagesWanted>
+// Cluster split-K variant: no workspace, one launch.  A cluster owns one
+// block of B and splits K over S slices; slice p accumulates K blocks
+// [p * kb_per, (p+1) * kb_per) into its own TMEM.  The grid is not
+// persistent: blocks x cluster-size CTAs, one work unit each.
+//   * one-CTA slices (kPair = false): the cluster is S CTAs (S = 1, 2, 4 or
+//     8, a launch attribute), the block is 128 rows of B, CTA r is slice r;
+//     tcgen05.mma.cta_group::1 M = 128, N = Mp.
+//   * pair slices (kPair): the cluster is S 2-CTA pairs (2S = 2, 4 or 8 CTAs;
+//     ranks 2p and 2p + 1 form pair p, the even rank leads), the block is 256
+//     rows of B, CTA half h = rank & 1 loads its 128 of them and rows
+//     [h Mp/2, (h+1) Mp/2) of A, and the pair leader issues
+//     tcgen05.mma.cta_group::2 M = 256, N = Mp.  Each SM then streams its
+//     rows of B but only half of A's slab: every SM's inflow (its TMA loads
+//     are capped at ~76 GB/s each, from L2 or DRAM) carries B + A/2 per K
+//     step instead of B + A, which is what bounds these kernels from M = 64 up.
+// The S partial sums of each row of C are added through distributed shared
+// memory (see the reduction below).
+template <int kMp, int kStagesWanted, bool kPair = false>
 struct SkinnyClusterCfg {
-  static constexpr int kRowsB = 128;
+  static_assert(!kPair || kMp >= 32, "pairs: each CTA holds Mp / 2 >= 16 rows of A");
+  static constexpr int kRowsB = 128;                      // rows of B per CTA
+  static constexpr int kRowsA = kPair ? kMp / 2 : kMp;    // rows of A per CTA
+  static constexpr int kBlockRows = kPair ? 2 * kRowsB : kRowsB;
   static constexpr int kSlabB = kRowsB * kSlabK * 2;      // 16 KiB
-  static constexpr int kSlabA = kMp * kSlabK * 2;
+  static constexpr int kSlabA = kRowsA * kSlabK * 2;
   static constexpr int kStageBytes = kSlabB + kSlabA;
   static constexpr int kChunk = kMp < 32 ? kMp : 32;      // rows of C reduced per pass
   static constexpr int kSlotBytes = kChunk * kRowsB * 4;  // [kChunk m][128 n] fp32
@@ -334,19 +345,19 @@ struct SkinnyClusterArgs {
   int M, N, K;
   int l2_hint;
   int k_blocks;       // ceil(K / 64)
-  int kb_per;         // K blocks per cluster rank
+  int kb_per;         // K blocks per slice
   int ldc;            // C row stride (elements)
   __nv_bfloat16* C;
   int* status;
   unsigned long long timeout_ns;
 };
 
-template <int kMp, int kStages>
+template <int kMp, int kStages, bool kPair = false>
 __global__ void __launch_bounds__(192)
 gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x K, box 64 x 128
-                           const __grid_constant__ CUtensorMap tmap_a,   // M x K, box 64 x Mp
+                           const __grid_constant__ CUtensorMap tmap_a,   // M x K, box 64 x Mp (pairs: Mp / 2)
                            const SkinnyClusterArgs args) {
-  using P = SkinnyClusterCfg<kMp, kStages>;
+  using P = SkinnyClusterCfg<kMp, kStages, kPair>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ alignas(8) uint64_t bar_full[kStages];
   __shared__ alignas(8) uint64_t bar_empty[kStages];
@@ -358,15 +369,20 @@ gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x 
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const uint32_t csize = cluster_nctarank();
+  const uint32_t half = kPair ? (rank & 1u) : 0u;      // this CTA's half of a pair block
+  const uint32_t leader = kPair ? (rank & ~1u) : rank;  // the pair's MMA issuer
+  const uint32_t slice = kPair ? (rank >> 1) : rank;   // K slice
+  const uint32_t slices = kPair ? (csize >> 1) : csize;
   const int tile = blockIdx.x / (int)csize;
-  const int kb0 = (int)rank * args.kb_per;
+  const int kb0 = (int)slice * args.kb_per;
   const int kb1 = kb0 + args.kb_per < args.k_blocks ? kb0 + args.kb_per : args.k_blocks;
+  const int row0 = tile * P::kBlockRows + (int)half * P::kRowsB;  // this CTA's first row of B
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t slot_base = smem_base + kStages * P::kStageBytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(smem_u32(&bar_full[s]), 1);
+      mbar_init(smem_u32(&bar_full[s]), kPair ? 2 : 1);  // pairs: both CTAs' bytes, in the leader
       mbar_init(smem_u32(&bar_empty[s]), 1);
     }
     mbar_init(smem_u32(&bar_acc_full), 1);
@@ -376,11 +392,18 @@ gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x 
     prefetch_tmap(&tmap_a);
   }
   if (warp == 1) {
-    tmem_alloc_1(smem_u32(&tmem_slot), P::kTmemAlloc);
-    tmem_relinquish_1();
+    if constexpr (kPair) {
+      tmem_alloc_pair(smem_u32(&tmem_slot), P::kTmemAlloc);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc_1(smem_u32(&tmem_slot), P::kTmemAlloc);
+      tmem_relinquish_1();
+    }
   }
   tc_fence_before_sync();
-  __syncthreads();
+  // Every CTA of the cluster has started and initialised its barriers before
+  // any peer signals them or writes its shared memory.
+  cluster_sync_all();
   tc_fence_after_sync();
   const uint32_t tmem_base = tmem_slot;
 
@@ -388,7 +411,7 @@ gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x 
   wctx.status = args.status;
   wctx.timeout_ns = args.timeout_ns;
   wctx.abort_local = smem_u32(&abort_word);
-  wctx.abort_peer = smem_u32(&abort_word);
+  wctx.abort_peer = kPair ? cluster_map(smem_u32(&abort_word), rank ^ 1u) : smem_u32(&abort_word);
 
   bool acc_ok = true;
   if (warp == 0) {
@@ -401,17 +424,30 @@ gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x 
         const int kb = skinny_kb(kb0, kb1 - kb0, i, tile, tiles);
         if (!wait_bounded(smem_u32(&bar_empty[stage]), phase ^ 1u, wctx, kErrWaitEmpty)) break;
         const uint32_t sb = smem_base + stage * P::kStageBytes;
-        const uint32_t fb = smem_u32(&bar_full[stage]);
-        mbar_arrive_expect_tx(fb, P::kStageBytes);
-        tma_load_2d_hint(sb, &tmap_b, kb * kSlabK, tile * P::kRowsB, fb, pol_b);
-        tma_load_2d_hint(sb + P::kSlabB, &tmap_a, kb * kSlabK, 0, fb, pol_a);
+        if constexpr (kPair) {
+          // The pair MMA commits a freed slot to the leader's empty barrier
+          // only; the leader's producer passes it on to its peer's.  (One
+          // commit arriving in both CTAs at once measured the same.)
+          if (half == 0 && i >= kStages)
+            mbar_arrive_cluster(cluster_map(smem_u32(&bar_empty[stage]), rank + 1u));
+          const uint32_t fb = cluster_map(smem_u32(&bar_full[stage]), leader);
+          mbar_arrive_expect_tx_cluster(fb, P::kStageBytes);
+          tma_load_2d_pair_hint(sb, &tmap_b, kb * kSlabK, row0, fb, pol_b);
+          tma_load_2d_pair_hint(sb + P::kSlabB, &tmap_a, kb * kSlabK, (int)half * P::kRowsA, fb,
+                                pol_a);
+        } else {
+          const uint32_t fb = smem_u32(&bar_full[stage]);
+          mbar_arrive_expect_tx(fb, P::kStageBytes);
+          tma_load_2d_hint(sb, &tmap_b, kb * kSlabK, row0, fb, pol_b);
+          tma_load_2d_hint(sb + P::kSlabB, &tmap_a, kb * kSlabK, 0, fb, pol_a);
+        }
         if (++stage == kStages) { stage = 0; phase ^= 1u; }
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_bf16_f32(P::kRowsB, kMp);
+    if (lane == 0 && half == 0) {
+      const uint32_t idesc = make_idesc_bf16_f32(P::kBlockRows, kMp);
       uint32_t stage = 0, phase = 0;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!wait_bounded(smem_u32(&bar_full[stage]), phase, wctx, kErrWaitFull)) break;
@@ -420,14 +456,27 @@ gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x 
         const uint64_t bdesc_big = make_sdesc_k128(sb);
         const uint64_t adesc_small = make_sdesc_k128(sb + P::kSlabB);
 #pragma unroll
-        for (int k = 0; k < kSlabK / kMmaK; ++k)
-          umma_bf16_1(tmem_base, bdesc_big + 2ull * k, adesc_small + 2ull * k, idesc,
-                      (kb != kb0 || k != 0) ? 1u : 0u);
-        umma_commit_1(smem_u32(&bar_empty[stage]));
+        for (int k = 0; k < kSlabK / kMmaK; ++k) {
+          const uint32_t acc = (kb != kb0 || k != 0) ? 1u : 0u;
+          if constexpr (kPair)
+            umma_bf16_pair(tmem_base, bdesc_big + 2ull * k, adesc_small + 2ull * k, idesc, acc);
+          else
+            umma_bf16_1(tmem_base, bdesc_big + 2ull * k, adesc_small + 2ull * k, idesc, acc);
+        }
+        if constexpr (kPair)
+          umma_commit_pair(cluster_map(smem_u32(&bar_empty[stage]), rank));
+        else
+          umma_commit_1(smem_u32(&bar_empty[stage]));
         if (++stage == kStages) { stage = 0; phase ^= 1u; }
       }
-      // Completes once every MMA above has (also when there were none).
-      umma_commit_1(smem_u32(&bar_acc_full));
+      // Each completes once every MMA above has (also when there were none);
+      // the epilogues of both halves wait for it before TMEM is read or freed.
+      if constexpr (kPair) {
+        umma_commit_pair(cluster_map(smem_u32(&bar_acc_full), rank));
+        umma_commit_pair(cluster_map(smem_u32(&bar_acc_full), rank + 1u));
+      } else {
+        umma_commit_1(smem_u32(&bar_acc_full));
+      }
     }
     __syncwarp();
   } else {
@@ -437,12 +486,24 @@ gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x 
     tc_fence_after_sync();
   }
 
-  // Cluster reduction, 32 (or Mp) rows of C per pass; all 6 warps take part
-  // in the cluster barriers, the 4 epilogue warps move the data.
-  const bool empty_slice = kb1 <= kb0;  // this rank saw no K blocks: its TMEM holds nothing
+  // Cross-slice reduction, kChunk (32, or Mp) rows of C per pass.  Row j of
+  // a chunk belongs to slice j % S, which keeps it as local row i = j / S of
+  // its slot (the slice's CTA of the same half).  Every slice pushes its
+  // partial of each row into the owner's slot, at [source slice][i][n]
+  // (fire-and-forget DSMEM stores, one cluster barrier makes them visible);
+  // the owner then adds the S partials of its rows from its own shared memory
+  // in slice order and stores them as bf16.  (Pulling the partials with
+  // remote loads instead paid a DSMEM round trip per row and slice: 5 us at
+  // Mp = 16 and 15 us at Mp = 64 on an 8192-row B.)  The slots are
+  // double-buffered, so one barrier per chunk suffices: a slice pushes into
+  // buffer (c & 1) only after the barrier of chunk c - 1, which every owner
+  // passes after its reads of chunk c - 2.  All 6 warps take part in the
+  // barriers; the 4 epilogue warps move the data.
+  const bool empty_slice = kb1 <= kb0;  // this slice saw no K blocks: its TMEM holds nothing
   const int quarter = warp & 3;
-  const int n_local = quarter * 32 + lane;       // row of B within the tile = column of C
-  const int n = tile * P::kRowsB + n_local;
+  const int n_local = quarter * 32 + lane;  // row of B within this CTA's 128 = column of C
+  const int n = row0 + n_local;
+  const int rows_per_slice = P::kChunk / (int)slices;  // slices <= 8 <= kChunk / 2
   for (int c = 0; c < kMp / P::kChunk; ++c) {
     const uint32_t slot = slot_base + (c & 1) * P::kSlotBytes;
     if (warp >= 2) {
@@ -459,30 +520,47 @@ gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x 
 #pragma unroll
         for (int j = 0; j < P::kChunk; ++j) v[j] = 0u;
       }
-      // slot[m][n_local]: consecutive lanes write consecutive words
+      // owner slot[slice][i][n_local]: consecutive lanes write consecutive words
 #pragma unroll
-      for (int j = 0; j < P::kChunk; ++j) st_shared_u32(slot + (j * P::kRowsB + n_local) * 4u, v[j]);
-    }
-    cluster_sync_all();
-    if (warp >= 2 && (c % (int)csize) == (int)rank && n < args.N) {
-      const int m0 = c * P::kChunk;
-#pragma unroll 4
       for (int j = 0; j < P::kChunk; ++j) {
-        if (m0 + j >= args.M) break;
-        const uint32_t off = slot + (j * P::kRowsB + n_local) * 4u;
-        float acc = 0.f;
-        for (uint32_t r = 0; r < csize; ++r) acc += ld_shared_cluster_f32(cluster_map(off, r));
-        args.C[(long long)(m0 + j) * args.ldc + n] = __float2bfloat16_rn(acc);
+        const uint32_t owner = (uint32_t)j % slices;
+        const uint32_t i = (uint32_t)j / slices;
+        const uint32_t off =
+            slot + ((slice * (uint32_t)rows_per_slice + i) * P::kRowsB + n_local) * 4u;
+        st_shared_cluster_u32(cluster_map(off, kPair ? 2u * owner + half : owner), v[j]);
       }
     }
     cluster_sync_all();
+    if (warp >= 2 && n < args.N) {
+      const int m0 = c * P::kChunk;
+#pragma unroll 1
+      for (int i = 0; i < rows_per_slice; ++i) {
+        const int m = m0 + (int)slice + i * (int)slices;
+        if (m >= args.M) break;
+        float acc = 0.f;
+        for (uint32_t r = 0; r < slices; ++r)
+          acc += ld_shared_f32(slot + ((r * (uint32_t)rows_per_slice + i) * P::kRowsB + n_local) * 4u);
+        args.C[(long long)m * args.ldc + n] = __float2bfloat16_rn(acc);
+      }
+    }
   }
 
   tc_fence_before_sync();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after_sync();
-    tmem_dealloc_1(tmem_base, P::kTmemAlloc);
+  if constexpr (kPair) {
+    // both CTAs of the pair are done with its TMEM before either frees it,
+    // and neither exits before the pair's deallocation has completed
+    cluster_sync_all();
+    if (warp == 1) {
+      tc_fence_after_sync();
+      tmem_dealloc_pair(tmem_base, P::kTmemAlloc);
+    }
+    cluster_sync_all();
+  } else {
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after_sync();
+      tmem_dealloc_1(tmem_base, P::kTmemAlloc);
+    }
   }
 }
 

@@ -98,8 +98,10 @@ int b200_gemm_get_splits(int M, int N, int K, int* splits);
  * single-launch cluster kernel for every M, 3 = the stream-K kernel for
  * every M, 4 = the stream-K kernel on 2-CTA pairs (each CTA loads 128 rows
  * of B and half of A's rows; tcgen05.mma.cta_group::2 reads both) for every
- * M.  Calls with a fused epilogue take the workspace kernel whatever the
- * mode.  No reference counterpart. */
+ * M, 5 = the cluster kernel on 2-CTA pairs (K split over the pairs of a
+ * cluster of 2, 4 or 8 CTAs, partials added in distributed shared memory)
+ * for every M.  Calls with a fused epilogue take the workspace kernel
+ * whatever the mode.  No reference counterpart. */
 int b200_gemm_set_skinny_mode(int mode);
 
 /* 128-row blocks of B per tile of the skinny stream-K kernel: 1, 2 (a

@@ -125,9 +125,9 @@ def test_ksplit_rejects_bad_arguments_without_a_device():
 
 def test_mode_setters_accept_their_range_and_reject_the_rest():
     lib = capi.lib()
-    for mode in range(5):                       # 4: stream-K on 2-CTA pairs
+    for mode in range(6):                       # 4, 5: stream-K / cluster on 2-CTA pairs
         assert lib.b200_gemm_set_skinny_mode(mode) == capi.OK
-    assert lib.b200_gemm_set_skinny_mode(5) == capi.ERR_INVALID_ARGUMENT
+    assert lib.b200_gemm_set_skinny_mode(6) == capi.ERR_INVALID_ARGUMENT
     assert lib.b200_gemm_set_skinny_mode(-1) == capi.ERR_INVALID_ARGUMENT
     capi.set_skinny_mode(1)
     for tiles in (0, 1, 2):

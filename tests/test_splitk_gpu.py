@@ -181,14 +181,14 @@ def test_k_split_and_row_shard_on_two_gpus():
 
 
 # ------------------------------------------------------- skinny-M kernel
-SKINNY_MODES = {"auto": 1, "cluster": 2, "stream": 3, "pair_stream": 4}
+SKINNY_MODES = {"auto": 1, "cluster": 2, "stream": 3, "pair_stream": 4, "pair_cluster": 5}
 
 
 @pytest.fixture(params=list(SKINNY_MODES))
 def skinny_mode(request):
     """The skinny path's kernels: chosen per shape, the cluster split-K kernel,
-    the stream-K kernel and the stream-K kernel on 2-CTA pairs, each forced for
-    every M."""
+    the stream-K kernel, and the stream-K and cluster kernels on 2-CTA pairs,
+    each forced for every M."""
     capi.set_skinny_mode(SKINNY_MODES[request.param])
     yield request.param
     capi.set_skinny_mode(1)
@@ -217,6 +217,25 @@ def test_skinny_kernel_forced_splits_random(splits):
     A, Bt = workloads.make_operands(M, N, K, seed=splits, weight_std=0.02)
     C = bf16_gemm(A, Bt)
     assert parity.passes(parity.metrics(C, A.float() @ Bt.float().T, A, Bt))
+
+
+@pytest.mark.parametrize("slices", [1, 2, 4])
+@pytest.mark.parametrize("M,N,K", [(64, 8192, 2048), (200, 4096, 4096), (40, 28672, 1024),
+                                   (256, 1280, 3008), (48, 2048, 520)])
+def test_skinny_pair_cluster_slices_exact_bits(M, N, K, slices):
+    """The cluster kernel on 2-CTA pairs with K split over 1, 2 and 4 pairs
+    (clusters of 2, 4 and 8 CTAs): whole and ragged pair blocks, grids of
+    more clusters than fit at once, and a slice left without K blocks (K =
+    520: 9 blocks over 4 slices of 3)."""
+    capi.set_skinny_mode(5)
+    capi.set_splits(slices)
+    try:
+        A, Bt = oracle.exact_inputs(M, N, K, seed=M + K)
+        C = bf16_gemm(dev(A), dev(Bt))
+        assert np.array_equal(bits(C), oracle.gemm_bf16(A, Bt))
+    finally:
+        capi.set_skinny_mode(1)
+        capi.set_splits(0)
 
 
 @pytest.mark.parametrize("mode", [3, 4], ids=["cta", "pair"])
