@@ -118,6 +118,15 @@ int dynamic_mode() {
 // Below this wave efficiency a 256 x 256 grid gets a stream-K tail (mode 1).
 constexpr double kStreamKWaveEfficiency = 0.97;
 
+// ... and only from this K up (mode 1): the tail's split tiles meet in a
+// fix-up whose cost a short tile does not repay.  Measured (cold L2,
+// TFLOP/s, 256-wide tiles with / without the tail): K = 1024: 4096 x 2048
+// 533 / 763, 4096 x 4096 795 / 1047, 8192 x 2048 791 / 1042; K = 2048: 2048
+// x 4096 878 / 1047; K = 3072: 4096 x 4096 1335 / 1360; K = 4096: 4096 x
+// 4096 1500 / 1457, 4096 x 2048 1305 / 1270, 8192 x 2048 1534 / 1457; K =
+// 8192: 4096 x 4096 1567 / 1491, 2048 x 4096 1503 / 1428.
+constexpr int kStreamKMinK = 4096;
+
 // Stream-K tail of the pair kernel: 0 = off, 1 = when the last wave of tiles
 // would leave pairs idle (default), 2 = whenever the tiles are not a whole
 // number of waves.  Initialised from B200_GEMM_STREAMK, changeable through
@@ -434,8 +443,13 @@ double wave_efficiency(long long tiles, int pairs) {
 // tile count costs wave efficiency or leaves pairs idle.  Grids of fewer
 // 256-wide tiles than pairs leave SMs idle while each pair walks the whole
 // K; 128- or 64-wide tiles then finish sooner: the width minimising
-// waves x width wins, the wider one on a tie.
-int choose_variant(int M, int N, const int* max_pairs) {
+// waves x width wins, the wider one on a tie.  Up to K = 1024 the 256-wide
+// tile is kept unless the 512-wide one is 2 % more wave-efficient: each
+// tile's mainloop is short, and only the 256-wide kernel hides a tile's
+// epilogue behind the next tile's MMAs (TFLOP/s, 256 / 512 wide at equal
+// wave counts: 4096 x 4096 x 1024 1047 / 982, 8192 x 2048 x 1024 1042 /
+// 960; at K = 2048, 8192 x 8192: 1616 / 1636).
+int choose_variant(int M, int N, int K, const int* max_pairs) {
   const int tn = tuning_tile_n();
   if (tn == 512) return kV512x64;
   if (tn == 128) return kV128x64;
@@ -464,9 +478,10 @@ int choose_variant(int M, int N, const int* max_pairs) {
   // pair busy to the end: count it as (nearly) full.
   double eff256 = wave_efficiency(t256, pairs(v256));
   if (stream_k_mode() != 0 && t256 > pairs(v256) && t256 % pairs(v256) != 0 &&
-      (stream_k_mode() == 2 || eff256 < kStreamKWaveEfficiency))
+      (stream_k_mode() == 2 || (eff256 < kStreamKWaveEfficiency && K >= kStreamKMinK)))
     eff256 = 0.99;
-  return wave_efficiency(t512, pairs(kV512x64)) + 0.02 >= eff256 ? kV512x64 : v256;
+  const double bias = K <= 1024 ? -0.02 : 0.02;
+  return wave_efficiency(t512, pairs(kV512x64)) + bias >= eff256 ? kV512x64 : v256;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -681,7 +696,8 @@ int launch_streamk(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   const long long tiles = (long long)args.tiles_m * ceil_div(args.N, C::kTileN);
   const int P = d.max_pairs[V];
   if (tiles <= P || tiles % P == 0) return B200_OK;
-  if (mode == 1 && wave_efficiency(tiles, P) >= kStreamKWaveEfficiency) return B200_OK;
+  if (mode == 1 && (wave_efficiency(tiles, P) >= kStreamKWaveEfficiency || args.K < kStreamKMinK))
+    return B200_OK;
   const long long k_blocks = ceil_div(args.K, C::kBK);
   args.dp_tiles = (int)(tiles / P * P);
   args.sk_tiles = (int)(tiles - args.dp_tiles);
@@ -1317,7 +1333,7 @@ int run_gemm(const void* A, const void* B, void* C, int M, int N, int K, int lda
     }
   }
   if (!kProfile && epi) return launch<false, kV256x64, kOutBf16Epi>(ta, tb, tc, args, 1, *d, stream);
-  return launch_bf16<kProfile>(choose_variant(M, N, d->max_pairs), ta, tb, tc, B, ldb, args, *d,
+  return launch_bf16<kProfile>(choose_variant(M, N, K, d->max_pairs), ta, tb, tc, B, ldb, args, *d,
                                stream);
 }
 
@@ -1576,7 +1592,7 @@ int run_ksplit(b200_ksplit_comm* c, const void* A, const void* B, void* C, int M
   DeviceState* d = nullptr;
   st = device_state(&d);
   if (st != B200_OK) return st;
-  const bool wide = choose_variant(M, N, d->max_pairs) == kV512x64;
+  const bool wide = choose_variant(M, N, K, d->max_pairs) == kV512x64;
   const long long pieces = ks_pieces(M, N, c->nranks, wide ? 2 * kSubN : kSubN);
   if (pieces > c->cap_pieces) return B200_ERR_TOO_LARGE;
   CUtensorMap ta, tb, tc;
@@ -1673,7 +1689,7 @@ int b200_gemm_launch_shape(int M, int N, int K, int* tiles, int* grid, int* smem
   if (M < 0 || N < 0 || K < 0) return B200_ERR_INVALID_ARGUMENT;
   DeviceState* d = nullptr;
   const bool have_dev = device_state(&d) == B200_OK;
-  const int v = choose_variant(M, N, have_dev ? d->max_pairs : nullptr);
+  const int v = choose_variant(M, N, K, have_dev ? d->max_pairs : nullptr);
   long long tile_n;
   int smem, thr;
   if (v == kV512x64) shape_of<kV512x64>(&tile_n, &smem, &thr);
@@ -2106,7 +2122,7 @@ int run_gemm_noalloc(const void* A, const void* B, void* C, int M, int N, int K,
   if (encode_2d(&tc, C, N, M, ldc, kStoreCols, 32) != B200_OK) return B200_ERR_TENSOR_MAP;
   // (no stream-K tail here: its slots, 74 pairs x 8 pieces x 32 KiB, exceed
   // the array's workspace)
-  return launch_bf16<false>(choose_variant(M, N, nd->launch.max_pairs), ta, tb, tc, B, ldb, args,
+  return launch_bf16<false>(choose_variant(M, N, K, nd->launch.max_pairs), ta, tb, tc, B, ldb, args,
                             nd->launch, stream, false);
 }
 

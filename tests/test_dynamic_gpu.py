@@ -40,7 +40,7 @@ def bits(C):
 
 @pytest.mark.parametrize("M,N,K,tile_n", [
     (4096, 4096, 1024, 256), (4096, 4096, 1024, 512), (2048, 2048, 2048, 128),
-    (2048, 2048, 1024, 64), (3000, 5000, 704, -1), (8192, 6144, 1024, -1),
+    (2048, 2048, 1024, 64), (3000, 5000, 704, -1), (8192, 6144, 4096, -1),
     (256, 2048, 8192, -1)])
 def test_dynamic_equals_static(M, N, K, tile_n):
     if capi.get_splits(M, N, K) > 1:
