@@ -117,8 +117,8 @@ int b200_gemm_set_skinny_tiles(int tiles);
  * evenly over all pairs; a tile cut between pairs is summed in the kernel by
  * the pair holding its last K blocks (fp32 pieces through a pool workspace,
  * one rounding).  0 = off, 1 = when the last wave would idle at least 3 % of
- * the pair-slots (default; B200_GEMM_STREAMK overrides), 2 = whenever the
- * last wave is partial.  The first stream-K call (pair tail or skinny
+ * the pair-slots and K >= 4096 (default; B200_GEMM_STREAMK overrides), 2 =
+ * whenever the last wave is partial, at any K.  The first stream-K call (pair tail or skinny
  * stream-K kernel) on each (device, stream) allocates that stream's flag
  * array with cudaMalloc, which may synchronise the device; it is cleared on
  * the stream itself.  No reference counterpart (the reference deals whole
