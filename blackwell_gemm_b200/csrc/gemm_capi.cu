@@ -812,25 +812,22 @@ int skc_slot(int M) {
                                                             : M <= 128 ? 6 : 7;
 }
 
-// The cluster kernel (mode 1) up to M = 128 where its grid of 128-row blocks
-// x S slices fits in one wave and each CTA's slice, (128 + Mp) rows of B and
-// A over K / S, stays within kClusterMaxSliceBytes.  It ends with one
-// distributed-shared-memory reduction (~1 us) where the stream-K kernel ends
-// with a global-memory fix-up of the blocks split between CTAs (~4 us), but
-// it streams with the CTAs of whole clusters (128 at N = 8192 or 4096)
-// rather than every SM, so it wins while slices are short.  Measured (cold
-// L2, median us, cluster / stream-K; after a written flush and after a flush
-// that leaves L2 clean): N = K = 8192: M = 16 (1.18 MB) 34.9 / 36.3, 31.8 /
-// 32.3; M = 32 (1.31 MB) 36.9 / 36.2, 33.6 / 33.0; M = 64 36.9 / 36.1 at best;
-// N = K = 4096: M = 32 18.5 / 21.8, 16.5 / 19.9; M = 64 20.6 / 22.1, 18.6 /
-// 21.8; M = 128 24.8 / 26.1, 24.5 / 24.7; N = 4096, K = 14336, M = 128 (1.8
-// MB) 39.5 / 39.8, 36.9 / 38.2.  With a forced slice count
-// (b200_gemm_set_splits) only M <= 8 takes it, as the split-K kernels do.
-constexpr double kClusterMaxSliceBytes = 1.2e6;
-
+// The cluster kernel (mode 1) wherever its grid of 128-row blocks x S
+// slices fits in one wave.  It ends with one distributed-shared-memory
+// reduction where the stream-K kernel ends with a global-memory fix-up of
+// the blocks split between CTAs, and it needs no workspace.  Measured (cold
+// L2, median us, after a flush that leaves L2 clean / after the written
+// flush; cluster, stream-K or split-K as chosen before, cuBLAS): N = K =
+// 8192: M = 16 30.7 / 32.9, 32.1 / 36.2, 28.7 / 37.0; M = 64 30.8 / 34.9,
+// 34.6 / 38.2, 29.2 / 37.8; M = 128 34.9 / 38.9, 40.1 / 42.3, 28.7 / 37.0;
+// N = K = 4096: M = 64 18.4 / 18.5, 21.7 / 22.7, 14.4 / 16.5; M = 256 28.7 /
+// 28.7, 30.9 / 33.0, 14.4 / 18.5; N = 4096, K = 14336: M = 128 32.9 / 35.0,
+// 38.1 / 40.2, 28.7 / 37.0.  Where the grid needs more than one wave (N =
+// 28672) the stream-K kernels stay ahead (M = 128: 61.4 / 65.6 against
+// 52.5 / 58.6).  With a forced slice count (b200_gemm_set_splits) only M <= 8
+// takes it, as the split-K kernels do.
 bool skinny_use_cluster(int M, int N, int K, const DeviceState* d) {
   if (tuning_splits() > 0) return M <= 8;
-  if (M > 128) return false;
   const int I = skc_slot(M);
   const long long tiles = ceil_div(N, 128);
   const int k_blocks = (int)ceil_div(K, kSlabK);
@@ -848,10 +845,28 @@ bool skinny_use_cluster(int M, int N, int K, const DeviceState* d) {
       }
     fit = 148 >> ci;
   }
-  if (tiles > fit) return false;
-  const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
-  const double slice = (128.0 + mp) * 2.0 * kSlabK * (double)ceil_div(k_blocks, 1 << ci);
-  return slice <= kClusterMaxSliceBytes;
+  return tiles <= fit;
+}
+
+// Above M = 128, the cluster kernel on 2-CTA pairs (each CTA loads half of
+// A's rows) where its grid of 256-row blocks fits in one wave on at least as
+// many CTAs as the one-CTA kernel's grid would use.  Measured as above (us):
+// M = 256, N = K = 8192 (both on 128 CTAs): pairs 42.1 / 43.1, one-CTA 45.0 /
+// 45.2, split-K 51.3 / 51.6, cuBLAS 34.7 / 43.1; N = 4096, K = 14336 (8-CTA
+// clusters of pairs do not fit: pairs on 64 CTAs, one-CTA on 128): pairs 53.2
+// / 55.3, one-CTA 45.1 / 47.1.
+bool skinny_use_pair_cluster(int M, int N, int K, const DeviceState* d) {
+  if (tuning_splits() > 0 || M <= 128 || d == nullptr) return false;
+  const int k_blocks = (int)ceil_div(K, kSlabK);
+  const int I = kSkcPair0 + 3;  // M > 128: Mp = 256
+  const long long tiles = ceil_div(N, 256);
+  const int ci = skc_choose(*d, I, true, tiles, k_blocks);
+  if (tiles > d->sk_clusters[I][ci]) return false;
+  const int I1 = skc_slot(M);
+  const long long tiles1 = ceil_div(N, 128);
+  const int ci1 = skc_choose(*d, I1, false, tiles1, k_blocks);
+  if (tiles1 > d->sk_clusters[I1][ci1]) return true;
+  return (tiles << ci) >= (tiles1 << ci1);
 }
 
 // Per shape (mode 1), without a forced slice count: the stream-K kernel
@@ -1175,12 +1190,22 @@ int run_skinny_cluster(const void* A, const void* B, void* C, int M, int N, int 
 int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int lda, int ldb,
                int ldc, DeviceState& d, cudaStream_t stream, const EpiArgs* epi = nullptr,
                const Scratch* scratch = nullptr) {
-  // Per shape (mode 1), up to 128 rows of A: the single-launch cluster
-  // kernel where its slices are short (skinny_use_cluster), else the
-  // stream-K kernel (all SMs, no workspace clear or rounding pass); above,
-  // the stream-K kernel on 2-CTA pairs for wide B, else the persistent
-  // split-K kernel.  B200_GEMM_SKINNY = 2..5 forces one kernel for every M.
+  // Per shape (mode 1): the single-launch cluster kernel, on 2-CTA pairs
+  // above 128 rows of A where that fits with two slices at most
+  // (skinny_use_pair_cluster), else on single CTAs where its grid fits one
+  // wave (skinny_use_cluster); otherwise up to 128 rows the stream-K kernel
+  // (all SMs, no workspace clear or rounding pass), above it the stream-K
+  // kernel on 2-CTA pairs for wide B, else the persistent split-K kernel.
+  // B200_GEMM_SKINNY = 2..5 forces one kernel for every M.  (The cluster
+  // kernel writes C directly, so fused epilogues take the workspace kernel,
+  // whose rounding pass applies them.)
   const int mode = skinny_mode();
+  if (epi == nullptr && mode == 1) {
+    if (skinny_use_pair_cluster(M, N, K, &d))
+      return run_skinny_cluster(A, B, C, M, N, K, lda, ldb, ldc, d, stream, true);
+    if (skinny_use_cluster(M, N, K, &d))
+      return run_skinny_cluster(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
+  }
   // (a forced slice count, b200_gemm_set_splits, takes the split-K kernels)
   const bool pair = mode == 4 || (mode == 1 && skinny_use_pair_stream(M, N, K));
   if (epi == nullptr && (mode == 3 || pair || (mode == 1 && skinny_use_stream(M, N, K, &d)))) {
@@ -1190,11 +1215,9 @@ int run_skinny(const void* A, const void* B, void* C, int M, int N, int K, int l
       default: return run_skinny_stream_slabs<2>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, scratch, pair);
     }
   }
-  // (The cluster kernel writes C directly, so fused epilogues take the
-  // workspace kernel, whose rounding pass applies them.)
   if (epi == nullptr && mode == 5)
     return run_skinny_cluster(A, B, C, M, N, K, lda, ldb, ldc, d, stream, true);
-  if (epi == nullptr && (mode == 2 || (mode == 1 && skinny_use_cluster(M, N, K, &d))))
+  if (epi == nullptr && mode == 2)
     return run_skinny_cluster(A, B, C, M, N, K, lda, ldb, ldc, d, stream);
   switch (skinny_slabs()) {
     case 1: return run_skinny_slabs<1>(A, B, C, M, N, K, lda, ldb, ldc, d, stream, epi, scratch);
@@ -1216,7 +1239,7 @@ int skinny_slices(int M, int N, int K, const DeviceState* d) {
   const int mode = skinny_mode();
   const int forced = tuning_splits();
   const long long tiles = ceil_div(N, 128);
-  if (d && mode == 5) {
+  if (d && (mode == 5 || (mode == 1 && skinny_use_pair_cluster(M, N, K, d)))) {
     const int I = kSkcPair0 + (M <= 32 ? 0 : M <= 64 ? 1 : M <= 128 ? 2 : 3);
     return (1 << skc_choose(*d, I, true, ceil_div(N, 256), (int)ceil_div(K, kSlabK))) / 2;
   }

@@ -332,10 +332,12 @@ struct SkinnyClusterCfg {
   static constexpr int kSlabB = kRowsB * kSlabK * 2;      // 16 KiB
   static constexpr int kSlabA = kRowsA * kSlabK * 2;
   static constexpr int kStageBytes = kSlabB + kSlabA;
-  static constexpr int kChunk = kMp < 32 ? kMp : 32;      // rows of C reduced per pass
-  static constexpr int kSlotBytes = kChunk * kRowsB * 4;  // [kChunk m][128 n] fp32
+  static constexpr int kChunk = kMp < 32 ? kMp : 32;      // accumulator columns per TMEM load
   static constexpr int kStages = kStagesWanted;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 2 * kSlotBytes + 1024;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
+  // the ring doubles as the reduction area: every slice's partial of every
+  // row of this CTA's 128 columns, 128 x Mp fp32
+  static_assert(kStages * kStageBytes >= kRowsB * kMp * 4, "ring too small to reduce in");
   static constexpr int kTmemAlloc = kMp <= 32 ? 32 : kMp;
   static constexpr int kThreads = 192;
   static_assert(kSmemBytes <= kSmemBudget - 1024, "does not fit in shared memory");
@@ -351,6 +353,94 @@ struct SkinnyClusterArgs {
   int* status;
   unsigned long long timeout_ns;
 };
+
+// The cluster kernel's cross-slice reduction, for S slices (a compile-time
+// count, so every register index below is static).  Rows of C (columns of
+// the accumulator) are dealt to the slices in contiguous blocks: slice o owns
+// rows [o R, (o+1) R), R = Mp / S.  Each slice's partials land in the owner's
+// shared memory laid out [source slice][lane quarter q][lane][row i of R]
+// fp32, so the rows one thread owes one owner are contiguous: it pushes them
+// with 16-byte DSMEM stores (8-byte for two rows) and the owner reads them
+// back with vector loads.  The 16-byte groups of a thread's rows are
+// permuted by lane (skc_group) so that the eight lanes of a quarter warp,
+// whose rows lie R x 4 bytes apart, hit eight different groups of banks.
+template <int kR>
+__device__ __forceinline__ uint32_t skc_group(int g, int lane) {
+  constexpr int kG = kR / 4;  // 16-byte groups per thread row
+  if constexpr (kG <= 1) {
+    return (uint32_t)g;
+  } else {
+    constexpr int kShift = kG >= 8 ? 0 : kG == 4 ? 1 : 2;
+    constexpr int kMask = (kG >= 8 ? 8 : kG) - 1;
+    return (uint32_t)(g ^ ((lane >> kShift) & kMask));
+  }
+}
+
+// Pushes columns [c0, c0 + kChunk) of this thread's accumulator row (v).
+template <int S, int kMp, int kChunk>
+__device__ __forceinline__ void skc_push(const uint32_t (&v)[kChunk], int c0, uint32_t area,
+                                         uint32_t slice, uint32_t half, bool pair, int q,
+                                         int lane) {
+  constexpr int kR = kMp / S;                      // rows per owner
+  constexpr int kRun = kR < kChunk ? kR : kChunk;  // contiguous rows per owner in this chunk
+  static_assert(kRun >= 2 && (kRun == 2 || kRun % 4 == 0), "rows per store run");
+  const uint32_t row_base =
+      area + (((slice * 4u + (uint32_t)q) * 32u + (uint32_t)lane) * kR) * 4u;
+#pragma unroll
+  for (int j0 = 0; j0 < kChunk; j0 += kRun) {
+    const int row = c0 + j0;  // first row of C of this run
+    const int o = row / kR, i0 = row % kR;
+    const uint32_t base =
+        cluster_map(row_base, pair ? 2u * (uint32_t)o + half : (uint32_t)o);
+    if constexpr (kRun == 2) {
+      st_shared_cluster_v2(base + 4u * (uint32_t)i0, v[j0], v[j0 + 1]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kRun; i += 4)
+        st_shared_cluster_v4(base + 16u * skc_group<kR>((i0 + i) / 4, lane), v[j0 + i],
+                             v[j0 + i + 1], v[j0 + i + 2], v[j0 + i + 3]);
+    }
+  }
+}
+
+// The owner's part: rows [slice R, (slice+1) R) of C at column n, each the
+// sum of the S slices' partials in slice order, stored as bf16.
+template <int S, int kMp>
+__device__ __forceinline__ void skc_finish(uint32_t area, uint32_t slice, int q, int lane, int n,
+                                           const SkinnyClusterArgs& args) {
+  constexpr int kR = kMp / S;
+  constexpr int kStep = kR == 2 ? 2 : 4;
+#pragma unroll 1
+  for (int i0 = 0; i0 < kR; i0 += kStep) {
+    float acc[kStep];
+#pragma unroll
+    for (int i = 0; i < kStep; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int r = 0; r < S; ++r) {
+      const uint32_t src =
+          area + ((((uint32_t)r * 4u + (uint32_t)q) * 32u + (uint32_t)lane) * kR) * 4u +
+          (kStep == 2 ? 4u * (uint32_t)i0 : 16u * skc_group<kR>(i0 / 4, lane));
+      if constexpr (kStep == 2) {
+        float a, b;
+        ld_shared_v2_f32(src, a, b);
+        acc[0] += a;
+        acc[1] += b;
+      } else {
+        float a, b, c, d;
+        ld_shared_v4_f32(src, a, b, c, d);
+        acc[0] += a;
+        acc[1] += b;
+        acc[2] += c;
+        acc[3] += d;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kStep; ++i) {
+      const int m = (int)slice * kR + i0 + i;
+      if (m < args.M) args.C[(long long)m * args.ldc + n] = __float2bfloat16_rn(acc[i]);
+    }
+  }
+}
 
 template <int kMp, int kStages, bool kPair = false>
 __global__ void __launch_bounds__(192)
@@ -378,7 +468,6 @@ gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x 
   const int kb1 = kb0 + args.kb_per < args.k_blocks ? kb0 + args.kb_per : args.k_blocks;
   const int row0 = tile * P::kBlockRows + (int)half * P::kRowsB;  // this CTA's first row of B
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const uint32_t slot_base = smem_base + kStages * P::kStageBytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -488,27 +577,24 @@ gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x 
     tc_fence_after_sync();
   }
 
-  // Cross-slice reduction, kChunk (32, or Mp) rows of C per pass.  Row j of
-  // a chunk belongs to slice j % S, which keeps it as local row i = j / S of
-  // its slot (the slice's CTA of the same half).  Every slice pushes its
-  // partial of each row into the owner's slot, at [source slice][i][n]
-  // (fire-and-forget DSMEM stores, one cluster barrier makes them visible);
-  // the owner then adds the S partials of its rows from its own shared memory
-  // in slice order and stores them as bf16.  (Pulling the partials with
-  // remote loads instead paid a DSMEM round trip per row and slice: 5 us at
-  // Mp = 16 and 15 us at Mp = 64 on an 8192-row B.)  The slots are
-  // double-buffered, so one barrier per chunk suffices: a slice pushes into
-  // buffer (c & 1) only after the barrier of chunk c - 1, which every owner
-  // passes after its reads of chunk c - 2.  All 6 warps take part in the
-  // barriers; the 4 epilogue warps move the data.
+  // Cross-slice reduction (skc_push / skc_finish).  Once every CTA of the
+  // cluster has seen its MMAs complete (first barrier), no operand load or
+  // MMA touches any ring any more, so the rings become the reduction area:
+  // every slice pushes all its partial rows into their owners' rings with
+  // fire-and-forget DSMEM stores, one barrier makes them visible, and each
+  // owner adds its rows' partials in slice order and stores them as bf16.
+  // (Earlier forms, on an 8192-row B: a remote load per row and slice, 5 us
+  // at Mp = 16 and 15 us at Mp = 64; 4-byte pushes in 32-row chunks with a
+  // barrier each, 6 and 12 us at Mp = 64 and 128.)  All 6 warps take part in
+  // the barriers; the 4 epilogue warps move the data.
   const bool empty_slice = kb1 <= kb0;  // this slice saw no K blocks: its TMEM holds nothing
   const int quarter = warp & 3;
   const int n_local = quarter * 32 + lane;  // row of B within this CTA's 128 = column of C
   const int n = row0 + n_local;
-  const int rows_per_slice = P::kChunk / (int)slices;  // slices <= 8 <= kChunk / 2
-  for (int c = 0; c < kMp / P::kChunk; ++c) {
-    const uint32_t slot = slot_base + (c & 1) * P::kSlotBytes;
-    if (warp >= 2) {
+  cluster_sync_all();
+  if (warp >= 2) {
+#pragma unroll 1
+    for (int c = 0; c < kMp / P::kChunk; ++c) {
       uint32_t v[P::kChunk];
       if (acc_ok && !empty_slice) {
         if constexpr (P::kChunk == 16)
@@ -522,28 +608,22 @@ gemm_skinny_cluster_kernel(const __grid_constant__ CUtensorMap tmap_b,   // N x 
 #pragma unroll
         for (int j = 0; j < P::kChunk; ++j) v[j] = 0u;
       }
-      // owner slot[slice][i][n_local]: consecutive lanes write consecutive words
-#pragma unroll
-      for (int j = 0; j < P::kChunk; ++j) {
-        const uint32_t owner = (uint32_t)j % slices;
-        const uint32_t i = (uint32_t)j / slices;
-        const uint32_t off =
-            slot + ((slice * (uint32_t)rows_per_slice + i) * P::kRowsB + n_local) * 4u;
-        st_shared_cluster_u32(cluster_map(off, kPair ? 2u * owner + half : owner), v[j]);
+      const int c0 = c * P::kChunk;
+      switch (slices) {
+        case 1: skc_push<1, kMp, P::kChunk>(v, c0, smem_base, slice, half, kPair, quarter, lane); break;
+        case 2: skc_push<2, kMp, P::kChunk>(v, c0, smem_base, slice, half, kPair, quarter, lane); break;
+        case 4: skc_push<4, kMp, P::kChunk>(v, c0, smem_base, slice, half, kPair, quarter, lane); break;
+        default: skc_push<8, kMp, P::kChunk>(v, c0, smem_base, slice, half, kPair, quarter, lane); break;
       }
     }
-    cluster_sync_all();
-    if (warp >= 2 && n < args.N) {
-      const int m0 = c * P::kChunk;
-#pragma unroll 1
-      for (int i = 0; i < rows_per_slice; ++i) {
-        const int m = m0 + (int)slice + i * (int)slices;
-        if (m >= args.M) break;
-        float acc = 0.f;
-        for (uint32_t r = 0; r < slices; ++r)
-          acc += ld_shared_f32(slot + ((r * (uint32_t)rows_per_slice + i) * P::kRowsB + n_local) * 4u);
-        args.C[(long long)m * args.ldc + n] = __float2bfloat16_rn(acc);
-      }
+  }
+  cluster_sync_all();
+  if (warp >= 2 && n < args.N) {
+    switch (slices) {
+      case 1: skc_finish<1, kMp>(smem_base, slice, quarter, lane, n, args); break;
+      case 2: skc_finish<2, kMp>(smem_base, slice, quarter, lane, n, args); break;
+      case 4: skc_finish<4, kMp>(smem_base, slice, quarter, lane, n, args); break;
+      default: skc_finish<8, kMp>(smem_base, slice, quarter, lane, n, args); break;
     }
   }
 

@@ -374,6 +374,28 @@ __device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uin
   asm volatile("st.shared::cluster.u32 [%0], %1;" :: "r"(cluster_addr), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ void st_shared_cluster_v2(uint32_t cluster_addr, uint32_t a,
+                                                     uint32_t b) {
+  asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" :: "r"(cluster_addr), "r"(a), "r"(b)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_shared_cluster_v4(uint32_t cluster_addr, uint32_t a,
+                                                     uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};"
+               :: "r"(cluster_addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__device__ __forceinline__ void ld_shared_v4_f32(uint32_t addr, float& a, float& b, float& c,
+                                                 float& d) {
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(a), "=f"(b), "=f"(c), "=f"(d) : "r"(addr) : "memory");
+}
+
+__device__ __forceinline__ void ld_shared_v2_f32(uint32_t addr, float& a, float& b) {
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(a), "=f"(b) : "r"(addr) : "memory");
+}
+
 __device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");

@@ -219,6 +219,19 @@ def test_skinny_kernel_forced_splits_random(splits):
     assert parity.passes(parity.metrics(C, A.float() @ Bt.float().T, A, Bt))
 
 
+@pytest.mark.parametrize("M,N,K", [(256, 8192, 2048), (200, 16384, 1024), (256, 4096, 14336)])
+def test_skinny_auto_takes_cluster_kernels_exact_bits(M, N, K):
+    """Per shape, above M = 128: the cluster kernel on 2-CTA pairs (two
+    slices at 8192 and one at 16384 rows of B) or on single CTAs (4096 rows
+    and K = 14336, where pairs would fill fewer SMs): exact results there."""
+    capi.set_skinny_mode(1)
+    capi.set_splits(0)
+    A, Bt = oracle.exact_inputs(M, N, K, seed=M + N)
+    C = bf16_gemm(dev(A), dev(Bt))
+    assert np.array_equal(bits(C), oracle.gemm_bf16(A, Bt))
+    assert capi.device_status(True) == 0
+
+
 @pytest.mark.parametrize("slices", [1, 2, 4])
 @pytest.mark.parametrize("M,N,K", [(64, 8192, 2048), (200, 4096, 4096), (40, 28672, 1024),
                                    (256, 1280, 3008), (48, 2048, 520)])
@@ -315,10 +328,11 @@ def test_skinny_stream_k_tiles_exact_bits(M, N, K, tiles):
         capi.set_skinny_tiles(0)
 
 
-@pytest.mark.parametrize("M,N,K", [(200, 24576, 1024), (256, 16384, 2048)])
+@pytest.mark.parametrize("M,N,K", [(200, 24576, 1024), (256, 40960, 1024)])
 def test_skinny_wide_n_takes_pair_stream_k_exact_bits(M, N, K):
-    """Above M = 128 with an fp32 workspace of 16 MB or more, the per-shape
-    choice runs the stream-K kernel on 2-CTA pairs: exact results there."""
+    """Above M = 128 with B too wide for one wave of cluster kernels and an
+    fp32 workspace of 16 MB or more, the per-shape choice runs the stream-K
+    kernel on 2-CTA pairs: exact results there."""
     capi.set_skinny_mode(1)
     A, Bt = oracle.exact_inputs(M, N, K, seed=M + 3)
     C = bf16_gemm(dev(A), dev(Bt))

@@ -16,15 +16,16 @@ from blackwell_gemm_b200 import capi, parity, workloads
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(256, 2048, 8192),     # split-K through the fixed workspace
-          (64, 8192, 8192),      # skinny stream-K: slots and flags in the array
+SHAPES = [(512, 1024, 8192),     # pair-kernel split-K: fp32 accumulator in the array
+          (16, 28672, 4096),     # skinny stream-K: slots and flags in the array
+          (150, 20480, 2048),    # skinny split-K: fp32 accumulator in the array
           (16, 8192, 8192),      # skinny cluster kernel (DSMEM reduction): no workspace
           (8, 4096, 4096),       # skinny cluster kernel, 4-CTA clusters
-          (256, 8192, 8192),     # skinny split-K: fp32 accumulator in the array
-          (128, 32768, 2048),    # skinny, slots too large for the array: cluster kernel
+          (256, 8192, 8192),     # skinny cluster kernel on 2-CTA pairs: no workspace
+          (128, 32768, 2048),    # skinny stream-K, slots too large for the array: cluster kernel
           (1024, 1024, 1024),    # not split: only the error word is used
           (300, 520, 4096),      # ragged
-          (4096, 4096, 4096)]    # the allocating path adds a stream-K tail, this one not
+          (4096, 4096, 4096)]    # the allocating path adds a stream-K tail, this one not    # the allocating path adds a stream-K tail, this one not
 
 
 def run(fn, A, Bt, C):
